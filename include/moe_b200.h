@@ -1,0 +1,179 @@
+/*
+ * moe_b200.h — C ABI of the B200 (sm_100a) MoE / SwitchGLU block.
+ *
+ * This library stands in for mlx-sys (crates/mlx-sys, bindgen over mlx-c) on the
+ * device-side MoE path of paulm17/mlx-rs. Each entry point names the reference
+ * interface it replaces (paths relative to the reference project).
+ *
+ * Conventions (mirroring crates/mlx-core/src/array.rs:43-49, where every mlx-c call
+ * returns an int and rc != 0 becomes Error::Mlx("<fn> failed (rc=N)")):
+ *   - every function returns MOE_OK (0) or a positive MOE_ERR_* code and never
+ *     aborts; moe_last_error() gives a one-line message for the last failure on
+ *     that context;
+ *   - all tensor arguments are DEVICE pointers owned by the caller, row-major and
+ *     contiguous; bf16 tensors are passed as void* (2-byte elements);
+ *   - optional arrays are NULL (as mlx-c's null ctx, crates/mlx-core/src/ops.rs:852-869);
+ *   - calls are asynchronous and ordered on the context's stream (MLX's lazy graph
+ *     + default stream, array.rs:28-40); the caller synchronises;
+ *   - scratch memory is owned by the context and grows on demand (moe_ctx_reserve
+ *     sizes it up front); a context must not be used by two threads at once.
+ *
+ * Quantized weights use the MLX affine layout (mlx_quantize, mode "affine"):
+ *   w      [rows, K * bits / 32] uint32, element e of a row is bits (e % (32/bits))*bits
+ *          of word e / (32/bits), lowest bits first;
+ *   scales [rows, K / group_size] bf16;  biases [rows, K / group_size] bf16 or NULL;
+ *   dequantised value = scale * q + bias.
+ * The CUDA kernels implement bits = 4 with group_size = 64 (the configuration of
+ * every model on this path); other valid MLX values return MOE_ERR_UNSUPPORTED.
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_B200_ABI_VERSION 1
+
+enum moe_status {
+    MOE_OK = 0,
+    MOE_ERR_INVALID = 1,     /* bad argument or shape */
+    MOE_ERR_UNSUPPORTED = 2, /* valid for MLX, not implemented by these kernels */
+    MOE_ERR_CUDA = 3,        /* a CUDA runtime call or kernel launch failed */
+    MOE_ERR_NO_MEMORY = 4,   /* scratch allocation failed */
+    MOE_ERR_TIMEOUT = 5      /* a bounded device-side wait gave up */
+};
+
+/* Router scoring (R2). */
+enum moe_scoring {
+    /* probs = softmax(logits): SparseMoeBlock::forward, qwen3_moe_python_port.rs:437 */
+    MOE_SCORING_SOFTMAX = 0,
+    /* probs = softmax(logits + expert_bias): MoeFeedForward::forward,
+     * lfm2_moe_python_port.rs:559-574 */
+    MOE_SCORING_SOFTMAX_BIAS = 1,
+    /* s = sigmoid(logits), select on s + expert_bias, weights from s (LFM2 sigmoid routing) */
+    MOE_SCORING_SIGMOID_BIAS_SELECT = 2
+};
+
+/* Block shape and options; the fields of Qwen3MoePythonPortConfig
+ * (qwen3_moe_python_port.rs:12-41) and Lfm2MoeConfig that the block reads. */
+typedef struct moe_block_config {
+    int32_t hidden;          /* H (hidden_size) */
+    int32_t num_experts;     /* E (num_experts), 1..512 */
+    int32_t top_k;           /* k (num_experts_per_tok), 1..32 */
+    int32_t moe_inter;       /* I (moe_intermediate_size) */
+    int32_t shared_inter;    /* Is (shared_expert_intermediate_size), 0 = none */
+    int32_t scoring;         /* enum moe_scoring */
+    int32_t norm_topk_prob;  /* renormalise the k selected weights to sum 1 */
+    int32_t has_shared_gate; /* sigmoid shared_expert_gate [1, H] present */
+    int32_t group_size;      /* quantization.group_size (64) */
+    int32_t bits;            /* quantization.bits (4) */
+} moe_block_config;
+
+/* One quantized matrix (a quantized mlx_nn::Linear without bias, linear.rs:117-139). */
+typedef struct moe_qweight {
+    const uint32_t* w;
+    const void* scales;
+    const void* biases; /* may be NULL */
+} moe_qweight;
+
+/* Device weights of one block: the stacked SwitchLinear tensors
+ * (qwen3_moe_python_port.rs:241-309, [E, N, K*bits/32]) or the pre-stacked
+ * switch_mlp tensors (lfm2_moe_python_port.rs:426-460). */
+typedef struct moe_block_weights {
+    moe_qweight router;             /* gate / router Linear: [E, H] */
+    const void* expert_bias;        /* [E] bf16, scoring modes 1 and 2 */
+    moe_qweight gate;               /* switch_mlp.gate_proj [E, I, H] */
+    moe_qweight up;                 /* switch_mlp.up_proj   [E, I, H] */
+    moe_qweight down;               /* switch_mlp.down_proj [E, H, I] */
+    moe_qweight shared_gate;        /* shared_expert.gate_proj [Is, H] */
+    moe_qweight shared_up;          /* shared_expert.up_proj   [Is, H] */
+    moe_qweight shared_down;        /* shared_expert.down_proj [H, Is] */
+    moe_qweight shared_expert_gate; /* shared_expert_gate [1, H] */
+} moe_block_weights;
+
+typedef struct moe_ctx moe_ctx;
+
+/* Context on a CUDA device and stream (cudaStream_t; NULL = the legacy default
+ * stream). Replaces the implicit mlx default device/stream of
+ * crates/mlx-core/src/array.rs:28-40 and stream.rs. */
+int moe_ctx_create(int device, void* stream, moe_ctx** out);
+void moe_ctx_destroy(moe_ctx* ctx);
+int moe_ctx_set_stream(moe_ctx* ctx, void* stream);
+/* Pre-size the context's scratch for blocks of this shape with up to max_tokens
+ * tokens, so later calls allocate nothing. */
+int moe_ctx_reserve(moe_ctx* ctx, const moe_block_config* cfg, int64_t max_tokens);
+/* Message of the last failed call on ctx ("" if none); valid until the next call. */
+const char* moe_last_error(const moe_ctx* ctx);
+int moe_abi_version(void);
+
+/*
+ * out[M, N] (bf16) = x[M, K] (bf16) . dequant(w)^T
+ * Replaces Array::quantized_matmul (crates/mlx-core/src/ops.rs:592-637), i.e.
+ * mlx_quantized_matmul(&out, x, w, scales, biases, transpose, gs, bits, "affine", s)
+ * at ops.rs:622-633, as called by Linear::forward (crates/mlx-nn/src/linear.rs:117-128).
+ * transpose must be nonzero (the only form the reference calls).
+ */
+int moe_quantized_matmul(moe_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w,
+                         const void* scales, const void* biases, int64_t N, int transpose,
+                         int group_size, int bits, void* out);
+
+/*
+ * out[i, N] (bf16) = x[row(i), K] . dequant(w[rhs_indices[i]])^T for i < batch,
+ * row(i) = lhs_indices ? lhs_indices[i] : i / x_repeat.
+ * Replaces Array::gather_qmm (crates/mlx-core/src/ops.rs:830-891), i.e.
+ * mlx_gather_qmm(&out, x, w, scales, biases, lhs, rhs, transpose, gs, bits, "affine",
+ * sorted_indices, s) at ops.rs:872-886, in the one-row-per-batch-element form that
+ * SwitchLinear::forward uses (qwen3_moe_python_port.rs:311-324,
+ * lfm2_moe_python_port.rs:462-479): x [T,1,1,K] against rhs [T,k] is x_rows = T,
+ * x_repeat = k; the down projection's x [T,k,1,I] is x_rows = T*k, x_repeat = 1.
+ * w is [num_experts, N, K*bits/32]. sorted_indices is accepted and ignored (the
+ * kernels always group rows by expert themselves). transpose must be nonzero.
+ */
+int moe_gather_qmm(moe_ctx* ctx, const void* x, int64_t x_rows, int64_t K, int64_t x_repeat,
+                   const uint32_t* lhs_indices, const uint32_t* w, const void* scales,
+                   const void* biases, int64_t num_experts, int64_t N,
+                   const uint32_t* rhs_indices, int64_t batch, int transpose, int group_size,
+                   int bits, int sorted_indices, void* out);
+
+/*
+ * out[rows, dim] = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * weight)
+ * Replaces Array::fast_rms_norm (crates/mlx-core/src/ops.rs:691-701) as called by
+ * RmsNorm::forward (crates/mlx-nn/src/rms_norm.rs:30-34). dim % 8 == 0.
+ */
+int moe_fast_rms_norm(moe_ctx* ctx, const void* x, const void* weight, float eps, int64_t rows,
+                      int64_t dim, void* out);
+
+/*
+ * The whole block: out[T, H] = MoE(x[T, H]) — router, scoring, top-k, SwitchGLU over
+ * the selected experts, weighted combine and the optional sigmoid-gated shared
+ * expert, on the context's stream.
+ * Replaces SparseMoeBlock::forward (qwen3_moe_python_port.rs:420-488) and
+ * MoeFeedForward::forward (lfm2_moe_python_port.rs:541-740), which are private in the
+ * reference and reach mlx-c through quantized_matmul / softmax / argpartition /
+ * take_along_axis / gather_qmm / multiply / sum_axis.
+ */
+int moe_block_forward(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts,
+                      const void* x, int64_t T, void* out);
+
+/*
+ * Routing only (R1-R4 plus the per-expert grouping gather_qmm forms internally):
+ *   idx[T, k] uint32      selected experts, by (score desc, index asc);
+ *   weights[T, k] bf16    combine weights (renormalised when norm_topk_prob);
+ *   offsets[E + 1] int32  exclusive prefix sum of per-expert pair counts;
+ *   perm[T * k] uint32    pairs p = t*k + j grouped by expert, ascending p within one.
+ * Any output pointer may be NULL. Replaces the router half of the block
+ * (qwen3_moe_python_port.rs:436-445, lfm2_moe_python_port.rs:559-586) and is what the
+ * reference's MLX_VALIDATE_MOE_DEVICE_ROUTER shadow check reads back (:449-464).
+ */
+int moe_block_route(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts,
+                    const void* x, int64_t T, uint32_t* idx, void* weights, int32_t* offsets,
+                    uint32_t* perm);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

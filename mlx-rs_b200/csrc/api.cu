@@ -1,0 +1,511 @@
+// api.cu — the extern "C" boundary declared in include/moe_b200.h.
+//
+// Validates arguments, owns the per-context scratch, and sequences the kernels of
+// the block on the context's stream:
+//   router logits (+ shared_expert_gate row) -> scoring / top-k / weights ->
+//   grouping by expert -> gate/up grouped GEMV with SwiGLU epilogue -> down grouped
+//   GEMV -> [shared expert gate/up, down] -> weighted combine (+ gated shared).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <new>
+#include <string>
+
+#include "../../include/moe_b200.h"
+#include "kernels.cuh"
+
+struct moe_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  std::string last_error;
+};
+
+namespace {
+
+constexpr int kGroupSeg = 1024;  // pairs per segment of the grouping sort
+
+int fail(moe_ctx* ctx, int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  if (ctx) ctx->last_error = buf;
+  return code;
+}
+
+#define MOE_CUDA(ctx, expr)                                                                       \
+  do {                                                                                            \
+    cudaError_t _e = (expr);                                                                      \
+    if (_e != cudaSuccess) return fail((ctx), MOE_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(_e)); \
+  } while (0)
+
+// Switches to the context's device for the duration of a call.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = true;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Bump allocator over the context scratch (256-byte aligned slices).
+struct Carve {
+  char* base;
+  size_t off = 0;
+  explicit Carve(void* b) : base(static_cast<char*>(b)) {}
+  template <class T>
+  T* take(size_t count) {
+    off = (off + 255) & ~size_t(255);
+    T* p = reinterpret_cast<T*>(base ? base + off : nullptr);
+    off += count * sizeof(T);
+    return p;
+  }
+};
+
+int ensure_scratch(moe_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->scratch_bytes) return MOE_OK;
+  if (ctx->scratch) {
+    // cudaFree waits for work in flight that may still use the old buffer.
+    cudaFree(ctx->scratch);
+    ctx->scratch = nullptr;
+    ctx->scratch_bytes = 0;
+  }
+  size_t want = std::max<size_t>(bytes, size_t(1) << 20);
+  cudaError_t e = cudaMalloc(&ctx->scratch, want);
+  if (e != cudaSuccess) {
+    ctx->scratch = nullptr;
+    return fail(ctx, MOE_ERR_NO_MEMORY, "scratch cudaMalloc(%zu) failed: %s", want, cudaGetErrorString(e));
+  }
+  ctx->scratch_bytes = want;
+  return MOE_OK;
+}
+
+int check_quant(moe_ctx* ctx, const char* fn, int64_t K, int group_size, int bits) {
+  if (!(bits == 2 || bits == 3 || bits == 4 || bits == 5 || bits == 6 || bits == 8))
+    return fail(ctx, MOE_ERR_INVALID, "%s: bits=%d is not a valid MLX affine width", fn, bits);
+  if (!(group_size == 32 || group_size == 64 || group_size == 128))
+    return fail(ctx, MOE_ERR_INVALID, "%s: group_size=%d is not a valid MLX group size", fn, group_size);
+  if (bits != 4 || group_size != 64)
+    return fail(ctx, MOE_ERR_UNSUPPORTED, "%s: only bits=4, group_size=64 are implemented (got %d, %d)", fn,
+                bits, group_size);
+  if (K <= 0 || K % 64 != 0)
+    return fail(ctx, MOE_ERR_INVALID, "%s: K=%lld must be a positive multiple of 64", fn, (long long)K);
+  return MOE_OK;
+}
+
+// Workspace of a block call with T tokens (base == null: size only).
+struct BlockWs {
+  uint16_t* logits;
+  uint32_t* idx;
+  uint16_t* wsel;
+  uint16_t* gate_val;
+  int32_t* hist;
+  int32_t* segbase;
+  int32_t* offsets;
+  int32_t* active;
+  int32_t* n_active;
+  uint32_t* perm;
+  uint32_t* inv;
+  uint16_t* hbuf;
+  uint16_t* ybuf;
+  uint16_t* hs;
+  uint16_t* ys;
+  size_t bytes;
+};
+
+BlockWs carve_block(void* base, const moe_block_config* c, int64_t T) {
+  Carve cv(base);
+  BlockWs w{};
+  const int64_t E = c->num_experts, P = T * c->top_k;
+  const int64_t nseg = std::max<int64_t>(1, (P + kGroupSeg - 1) / kGroupSeg);
+  w.logits = cv.take<uint16_t>(T * (E + 1));
+  w.idx = cv.take<uint32_t>(P);
+  w.wsel = cv.take<uint16_t>(P);
+  w.gate_val = cv.take<uint16_t>(T);
+  w.hist = cv.take<int32_t>(nseg * E);
+  w.segbase = cv.take<int32_t>(nseg * E);
+  w.offsets = cv.take<int32_t>(E + 1);
+  w.active = cv.take<int32_t>(E);
+  w.n_active = cv.take<int32_t>(1);
+  w.perm = cv.take<uint32_t>(P);
+  w.inv = cv.take<uint32_t>(P);
+  w.hbuf = cv.take<uint16_t>(P * c->moe_inter);
+  w.ybuf = cv.take<uint16_t>(P * c->hidden);
+  if (c->shared_inter > 0) {
+    w.hs = cv.take<uint16_t>(T * c->shared_inter);
+    w.ys = cv.take<uint16_t>(T * c->hidden);
+  }
+  w.bytes = cv.off + 256;
+  return w;
+}
+
+int check_block(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* w, const char* fn) {
+  if (!c) return fail(ctx, MOE_ERR_INVALID, "%s: null config", fn);
+  int rc = check_quant(ctx, fn, c->hidden, c->group_size, c->bits);
+  if (rc) return rc;
+  if (c->num_experts <= 0 || c->num_experts > 512)
+    return fail(ctx, MOE_ERR_UNSUPPORTED, "%s: num_experts=%d (supported 1..512)", fn, c->num_experts);
+  if (c->top_k <= 0 || c->top_k > 32 || c->top_k > c->num_experts)
+    return fail(ctx, MOE_ERR_INVALID, "%s: top_k=%d (1..min(32, num_experts))", fn, c->top_k);
+  if (c->moe_inter <= 0 || c->moe_inter % 64 != 0)
+    return fail(ctx, MOE_ERR_INVALID, "%s: moe_inter=%d must be a positive multiple of 64", fn, c->moe_inter);
+  if (c->shared_inter < 0 || c->shared_inter % 64 != 0)
+    return fail(ctx, MOE_ERR_INVALID, "%s: shared_inter=%d must be a multiple of 64", fn, c->shared_inter);
+  if (c->scoring < 0 || c->scoring > 2) return fail(ctx, MOE_ERR_INVALID, "%s: scoring=%d", fn, c->scoring);
+  if (!w) return fail(ctx, MOE_ERR_INVALID, "%s: null weights", fn);
+  if (!w->router.w || !w->router.scales) return fail(ctx, MOE_ERR_INVALID, "%s: router weight missing", fn);
+  if (c->scoring != MOE_SCORING_SOFTMAX && !w->expert_bias)
+    return fail(ctx, MOE_ERR_INVALID, "%s: scoring mode %d needs expert_bias", fn, c->scoring);
+  const moe_qweight* need[3] = {&w->gate, &w->up, &w->down};
+  for (const moe_qweight* q : need)
+    if (!q->w || !q->scales) return fail(ctx, MOE_ERR_INVALID, "%s: expert weights missing", fn);
+  if (c->shared_inter > 0) {
+    const moe_qweight* sh[3] = {&w->shared_gate, &w->shared_up, &w->shared_down};
+    for (const moe_qweight* q : sh)
+      if (!q->w || !q->scales) return fail(ctx, MOE_ERR_INVALID, "%s: shared expert weights missing", fn);
+    if (c->has_shared_gate && (!w->shared_expert_gate.w || !w->shared_expert_gate.scales))
+      return fail(ctx, MOE_ERR_INVALID, "%s: shared_expert_gate weight missing", fn);
+  }
+  const void* ptrs[] = {w->router.w, w->gate.w, w->up.w, w->down.w};
+  for (const void* p : ptrs)
+    if (!aligned16(p)) return fail(ctx, MOE_ERR_INVALID, "%s: weight pointers must be 16-byte aligned", fn);
+  return MOE_OK;
+}
+
+// Routing + grouping of one block call into ws.
+int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* w, const void* x, int64_t T,
+              const BlockWs& ws) {
+  const int E = c->num_experts;
+  const bool gate_row = c->shared_inter > 0 && c->has_shared_gate;
+  moe::RouterArgs ra{};
+  ra.x = static_cast<const uint16_t*>(x);
+  ra.T = (int)T;
+  ra.K = c->hidden;
+  ra.E = E;
+  ra.n_rows = E + (gate_row ? 1 : 0);
+  ra.group_size = c->group_size;
+  ra.w = w->router.w;
+  ra.s = static_cast<const uint16_t*>(w->router.scales);
+  ra.b = static_cast<const uint16_t*>(w->router.biases);
+  ra.gate_w = w->shared_expert_gate.w;
+  ra.gate_s = static_cast<const uint16_t*>(w->shared_expert_gate.scales);
+  ra.gate_b = static_cast<const uint16_t*>(w->shared_expert_gate.biases);
+  ra.logits = ws.logits;
+  MOE_CUDA(ctx, moe::launch_router(ra, ctx->stream));
+
+  moe::TopkArgs ta{};
+  ta.logits = ws.logits;
+  ta.T = (int)T;
+  ta.E = E;
+  ta.n_rows = ra.n_rows;
+  ta.k = c->top_k;
+  ta.scoring = c->scoring;
+  ta.norm_topk_prob = c->norm_topk_prob;
+  ta.expert_bias = static_cast<const uint16_t*>(w->expert_bias);
+  ta.idx = ws.idx;
+  ta.weights = ws.wsel;
+  ta.gate_val = gate_row ? ws.gate_val : nullptr;
+  MOE_CUDA(ctx, moe::launch_topk(ta, ctx->stream));
+
+  moe::GroupArgs ga{};
+  ga.key = ws.idx;
+  ga.P = T * c->top_k;
+  ga.E = E;
+  ga.seg = kGroupSeg;
+  ga.nseg = (int)std::max<int64_t>(1, (ga.P + kGroupSeg - 1) / kGroupSeg);
+  ga.hist = ws.hist;
+  ga.segbase = ws.segbase;
+  ga.offsets = ws.offsets;
+  ga.active = ws.active;
+  ga.n_active = ws.n_active;
+  ga.perm = ws.perm;
+  ga.inv = ws.inv;
+  MOE_CUDA(ctx, moe::launch_group(ga, ctx->stream));
+  return MOE_OK;
+}
+
+moe::QgemvArgs qgemv_args(const moe_qweight& m0, const moe_qweight* m1, int N, int K) {
+  moe::QgemvArgs q{};
+  q.w0 = m0.w;
+  q.s0 = static_cast<const uint16_t*>(m0.scales);
+  q.b0 = static_cast<const uint16_t*>(m0.biases);
+  if (m1) {
+    q.w1 = m1->w;
+    q.s1 = static_cast<const uint16_t*>(m1->scales);
+    q.b1 = static_cast<const uint16_t*>(m1->biases);
+  }
+  q.N = N;
+  q.K = K;
+  return q;
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_abi_version(void) { return MOE_B200_ABI_VERSION; }
+
+int moe_ctx_create(int device, void* stream, moe_ctx** out) {
+  if (!out) return MOE_ERR_INVALID;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return MOE_ERR_CUDA;
+  moe_ctx* c = new (std::nothrow) moe_ctx();
+  if (!c) return MOE_ERR_NO_MEMORY;
+  c->device = device;
+  c->stream = static_cast<cudaStream_t>(stream);
+  *out = c;
+  return MOE_OK;
+}
+
+void moe_ctx_destroy(moe_ctx* ctx) {
+  if (!ctx) return;
+  if (ctx->scratch) {
+    DeviceGuard g(ctx->device);
+    cudaFree(ctx->scratch);
+  }
+  delete ctx;
+}
+
+int moe_ctx_set_stream(moe_ctx* ctx, void* stream) {
+  if (!ctx) return MOE_ERR_INVALID;
+  ctx->stream = static_cast<cudaStream_t>(stream);
+  return MOE_OK;
+}
+
+const char* moe_last_error(const moe_ctx* ctx) { return ctx ? ctx->last_error.c_str() : "null context"; }
+
+int moe_ctx_reserve(moe_ctx* ctx, const moe_block_config* cfg, int64_t max_tokens) {
+  if (!ctx) return MOE_ERR_INVALID;
+  ctx->last_error.clear();
+  if (!cfg || max_tokens < 0) return fail(ctx, MOE_ERR_INVALID, "moe_ctx_reserve: bad arguments");
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  return ensure_scratch(ctx, carve_block(nullptr, cfg, max_tokens).bytes);
+}
+
+int moe_quantized_matmul(moe_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w,
+                         const void* scales, const void* biases, int64_t N, int transpose, int group_size,
+                         int bits, void* out) {
+  if (!ctx) return MOE_ERR_INVALID;
+  ctx->last_error.clear();
+  const char* fn = "moe_quantized_matmul";
+  int rc = check_quant(ctx, fn, K, group_size, bits);
+  if (rc) return rc;
+  if (!transpose) return fail(ctx, MOE_ERR_UNSUPPORTED, "%s: transpose=false is not implemented", fn);
+  if (M < 0 || N <= 0 || N > INT32_MAX || M > INT32_MAX) return fail(ctx, MOE_ERR_INVALID, "%s: bad M/N", fn);
+  if (M == 0) return MOE_OK;
+  if (!x || !w || !scales || !out) return fail(ctx, MOE_ERR_INVALID, "%s: null pointer", fn);
+  if (!aligned16(x) || !aligned16(w)) return fail(ctx, MOE_ERR_INVALID, "%s: x and w must be 16-byte aligned", fn);
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  moe_qweight m{w, scales, biases};
+  moe::QgemvArgs q = qgemv_args(m, nullptr, (int)N, (int)K);
+  q.x = static_cast<const uint16_t*>(x);
+  q.x_mode = 0;
+  q.n_identity = (int)M;
+  q.out = static_cast<uint16_t*>(out);
+  MOE_CUDA(ctx, moe::launch_qgemv(q, false, 1, (int)std::min<int64_t>(M, 16), ctx->stream));
+  return MOE_OK;
+}
+
+int moe_gather_qmm(moe_ctx* ctx, const void* x, int64_t x_rows, int64_t K, int64_t x_repeat,
+                   const uint32_t* lhs_indices, const uint32_t* w, const void* scales, const void* biases,
+                   int64_t num_experts, int64_t N, const uint32_t* rhs_indices, int64_t batch, int transpose,
+                   int group_size, int bits, int sorted_indices, void* out) {
+  (void)sorted_indices;
+  (void)x_rows;
+  if (!ctx) return MOE_ERR_INVALID;
+  ctx->last_error.clear();
+  const char* fn = "moe_gather_qmm";
+  int rc = check_quant(ctx, fn, K, group_size, bits);
+  if (rc) return rc;
+  if (!transpose) return fail(ctx, MOE_ERR_UNSUPPORTED, "%s: transpose=false is not implemented", fn);
+  if (batch < 0 || N <= 0 || N > INT32_MAX || num_experts <= 0 || num_experts > 4096 || batch > INT32_MAX)
+    return fail(ctx, MOE_ERR_INVALID, "%s: bad batch/N/num_experts", fn);
+  if (!lhs_indices && x_repeat <= 0) return fail(ctx, MOE_ERR_INVALID, "%s: x_repeat must be positive", fn);
+  if (batch == 0) return MOE_OK;
+  if (!x || !w || !scales || !rhs_indices || !out) return fail(ctx, MOE_ERR_INVALID, "%s: null pointer", fn);
+  if (!aligned16(x) || !aligned16(w)) return fail(ctx, MOE_ERR_INVALID, "%s: x and w must be 16-byte aligned", fn);
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+
+  const int E = (int)num_experts;
+  const int64_t nseg = std::max<int64_t>(1, (batch + kGroupSeg - 1) / kGroupSeg);
+  Carve size_only(nullptr);
+  size_only.take<int32_t>(nseg * E);
+  size_only.take<int32_t>(nseg * E);
+  size_only.take<int32_t>(E + 1);
+  size_only.take<int32_t>(E);
+  size_only.take<int32_t>(1);
+  size_only.take<uint32_t>(batch);
+  rc = ensure_scratch(ctx, size_only.off + 256);
+  if (rc) return rc;
+  Carve cv(ctx->scratch);
+  moe::GroupArgs ga{};
+  ga.key = rhs_indices;
+  ga.P = batch;
+  ga.E = E;
+  ga.seg = kGroupSeg;
+  ga.nseg = (int)nseg;
+  ga.hist = cv.take<int32_t>(nseg * E);
+  ga.segbase = cv.take<int32_t>(nseg * E);
+  ga.offsets = cv.take<int32_t>(E + 1);
+  ga.active = cv.take<int32_t>(E);
+  ga.n_active = cv.take<int32_t>(1);
+  ga.perm = cv.take<uint32_t>(batch);
+  ga.inv = nullptr;
+  MOE_CUDA(ctx, moe::launch_group(ga, ctx->stream));
+
+  moe_qweight m{w, scales, biases};
+  moe::QgemvArgs q = qgemv_args(m, nullptr, (int)N, (int)K);
+  q.x = static_cast<const uint16_t*>(x);
+  q.x_mode = lhs_indices ? 2 : 1;
+  q.x_repeat = (int)std::max<int64_t>(1, x_repeat);
+  q.lhs = lhs_indices;
+  q.perm = ga.perm;
+  q.offsets = ga.offsets;
+  q.active = ga.active;
+  q.n_active = ga.n_active;
+  q.out = static_cast<uint16_t*>(out);
+  q.out_mode = 1;
+  const int slots = (int)std::min<int64_t>(batch, E);
+  MOE_CUDA(ctx, moe::launch_qgemv(q, false, slots, (int)std::min<int64_t>(batch, 16), ctx->stream));
+  return MOE_OK;
+}
+
+int moe_fast_rms_norm(moe_ctx* ctx, const void* x, const void* weight, float eps, int64_t rows, int64_t dim,
+                      void* out) {
+  if (!ctx) return MOE_ERR_INVALID;
+  ctx->last_error.clear();
+  if (rows < 0 || dim <= 0 || dim % 8 != 0 || dim > INT32_MAX)
+    return fail(ctx, MOE_ERR_INVALID, "moe_fast_rms_norm: dim=%lld must be a positive multiple of 8", (long long)dim);
+  if (rows == 0) return MOE_OK;
+  if (!x || !weight || !out || !aligned16(x) || !aligned16(weight) || !aligned16(out))
+    return fail(ctx, MOE_ERR_INVALID, "moe_fast_rms_norm: pointers must be non-null and 16-byte aligned");
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  MOE_CUDA(ctx, moe::launch_rms_norm(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(weight), eps, rows,
+                                     (int)dim, static_cast<uint16_t*>(out), ctx->stream));
+  return MOE_OK;
+}
+
+int moe_block_route(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x,
+                    int64_t T, uint32_t* idx, void* weights, int32_t* offsets, uint32_t* perm) {
+  if (!ctx) return MOE_ERR_INVALID;
+  ctx->last_error.clear();
+  int rc = check_block(ctx, cfg, wts, "moe_block_route");
+  if (rc) return rc;
+  if (T < 0 || T > (INT32_MAX / 64)) return fail(ctx, MOE_ERR_INVALID, "moe_block_route: bad T");
+  if (T == 0) return MOE_OK;
+  if (!x || !aligned16(x)) return fail(ctx, MOE_ERR_INVALID, "moe_block_route: x must be 16-byte aligned");
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  rc = ensure_scratch(ctx, carve_block(nullptr, cfg, T).bytes);
+  if (rc) return rc;
+  BlockWs ws = carve_block(ctx->scratch, cfg, T);
+  rc = run_route(ctx, cfg, wts, x, T, ws);
+  if (rc) return rc;
+  const int64_t P = T * cfg->top_k;
+  if (idx) MOE_CUDA(ctx, cudaMemcpyAsync(idx, ws.idx, P * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  if (weights) MOE_CUDA(ctx, cudaMemcpyAsync(weights, ws.wsel, P * 2, cudaMemcpyDeviceToDevice, ctx->stream));
+  if (offsets)
+    MOE_CUDA(ctx, cudaMemcpyAsync(offsets, ws.offsets, (cfg->num_experts + 1) * 4, cudaMemcpyDeviceToDevice,
+                                  ctx->stream));
+  if (perm) MOE_CUDA(ctx, cudaMemcpyAsync(perm, ws.perm, P * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  return MOE_OK;
+}
+
+int moe_block_forward(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x,
+                      int64_t T, void* out) {
+  if (!ctx) return MOE_ERR_INVALID;
+  ctx->last_error.clear();
+  const char* fn = "moe_block_forward";
+  int rc = check_block(ctx, cfg, wts, fn);
+  if (rc) return rc;
+  if (T < 0 || T > (INT32_MAX / 64)) return fail(ctx, MOE_ERR_INVALID, "%s: bad T", fn);
+  if (T == 0) return MOE_OK;
+  if (!x || !out || !aligned16(x) || !aligned16(out))
+    return fail(ctx, MOE_ERR_INVALID, "%s: x and out must be non-null and 16-byte aligned", fn);
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  rc = ensure_scratch(ctx, carve_block(nullptr, cfg, T).bytes);
+  if (rc) return rc;
+  BlockWs ws = carve_block(ctx->scratch, cfg, T);
+  rc = run_route(ctx, cfg, wts, x, T, ws);
+  if (rc) return rc;
+
+  const int E = cfg->num_experts, H = cfg->hidden, I = cfg->moe_inter, k = cfg->top_k;
+  const int64_t P = T * k;
+  const int slots = (int)std::min<int64_t>(P, E);
+  const int max_rows = (int)std::min<int64_t>(T, 16);
+
+  // SwitchGLU gate/up + SiLU*up over grouped rows (x row = pair / k).
+  moe::QgemvArgs gu = qgemv_args(wts->gate, &wts->up, I, H);
+  gu.x = static_cast<const uint16_t*>(x);
+  gu.x_mode = 1;
+  gu.x_repeat = k;
+  gu.perm = ws.perm;
+  gu.offsets = ws.offsets;
+  gu.active = ws.active;
+  gu.n_active = ws.n_active;
+  gu.out = ws.hbuf;
+  gu.out_mode = 0;
+  MOE_CUDA(ctx, moe::launch_qgemv(gu, true, slots, max_rows, ctx->stream));
+
+  // down projection over the same grouped rows.
+  moe::QgemvArgs dn = qgemv_args(wts->down, nullptr, H, I);
+  dn.x = ws.hbuf;
+  dn.x_mode = 0;
+  dn.perm = ws.perm;
+  dn.offsets = ws.offsets;
+  dn.active = ws.active;
+  dn.n_active = ws.n_active;
+  dn.out = ws.ybuf;
+  dn.out_mode = 0;
+  MOE_CUDA(ctx, moe::launch_qgemv(dn, false, slots, max_rows, ctx->stream));
+
+  const bool shared = cfg->shared_inter > 0;
+  if (shared) {
+    const int Is = cfg->shared_inter;
+    moe::QgemvArgs sgu = qgemv_args(wts->shared_gate, &wts->shared_up, Is, H);
+    sgu.x = static_cast<const uint16_t*>(x);
+    sgu.x_mode = 0;
+    sgu.n_identity = (int)T;
+    sgu.out = ws.hs;
+    MOE_CUDA(ctx, moe::launch_qgemv(sgu, true, 1, max_rows, ctx->stream));
+    moe::QgemvArgs sdn = qgemv_args(wts->shared_down, nullptr, H, Is);
+    sdn.x = ws.hs;
+    sdn.x_mode = 0;
+    sdn.n_identity = (int)T;
+    sdn.out = ws.ys;
+    MOE_CUDA(ctx, moe::launch_qgemv(sdn, false, 1, max_rows, ctx->stream));
+  }
+
+  moe::CombineArgs ca{};
+  ca.y = ws.ybuf;
+  ca.inv = ws.inv;
+  ca.weights = ws.wsel;
+  ca.shared = shared ? ws.ys : nullptr;
+  ca.gate_val = (shared && cfg->has_shared_gate) ? ws.gate_val : nullptr;
+  ca.T = (int)T;
+  ca.k = k;
+  ca.H = H;
+  ca.out = static_cast<uint16_t*>(out);
+  MOE_CUDA(ctx, moe::launch_combine(ca, ctx->stream));
+  return MOE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,113 @@
+// combine.cu — weighted combine of the k expert outputs (+ gated shared expert) and RMSNorm.
+//
+// combine: out[t] = bf16( sum_j bf16(y[t,j] * w[t,j]) ), fp32 sum over j = 0..k-1 in
+// index order (expert_out.multiply(score).sum_axis(1), qwen3_moe_python_port.rs:471-472;
+// lfm2_moe_python_port.rs:718-732), then, with a shared expert,
+// out = bf16(out + bf16(shared * bf16(sigmoid(gate_logit)))) (:477-484).
+// Each thread owns 8 consecutive hidden elements of one token (16-byte loads/stores).
+//
+// rms_norm: y = bf16(bf16(x * r) * w), r = 1 / sqrt(sum(x^2) / dim + eps) with IEEE
+// sqrt and divide; sum(x^2) in the canonical order (lane l of a warp owns the chunks
+// of 8 elements c = l, l+32, ..., fma per element, then the xor butterfly), which the
+// CPU oracle evaluates identically. RmsNorm::forward, crates/mlx-nn/src/rms_norm.rs:30-34.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace moe {
+
+__global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
+  const int vec_per_row = a.H >> 3;
+  const int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (id >= (int64_t)a.T * vec_per_row) return;
+  const int t = (int)(id / vec_per_row);
+  const int h = (int)(id - (int64_t)t * vec_per_row) * 8;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+  for (int j = 0; j < a.k; ++j) {
+    const int64_t p = (int64_t)t * a.k + j;
+    const float wj = bf2f(a.weights[p]);
+    const uint4 v = *reinterpret_cast<const uint4*>(a.y + (size_t)a.inv[p] * a.H + h);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      acc[2 * i] = __fadd_rn(acc[2 * i], rbf(__fmul_rn(bf_lo(u[i]), wj)));
+      acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], rbf(__fmul_rn(bf_hi(u[i]), wj)));
+    }
+  }
+  uint16_t o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = f2bf(acc[i]);
+  if (a.shared) {
+    const uint4 v = *reinterpret_cast<const uint4*>(a.shared + (size_t)t * a.H + h);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    const bool gated = a.gate_val != nullptr;
+    const float gv = gated ? bf2f(a.gate_val[t]) : 1.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float s = (i & 1) ? bf_hi(u[i >> 1]) : bf_lo(u[i >> 1]);
+      if (gated) s = rbf(__fmul_rn(s, gv));
+      o[i] = f2bf(__fadd_rn(bf2f(o[i]), s));
+    }
+  }
+  uint4 ov;
+  ov.x = (uint32_t)o[0] | ((uint32_t)o[1] << 16);
+  ov.y = (uint32_t)o[2] | ((uint32_t)o[3] << 16);
+  ov.z = (uint32_t)o[4] | ((uint32_t)o[5] << 16);
+  ov.w = (uint32_t)o[6] | ((uint32_t)o[7] << 16);
+  *reinterpret_cast<uint4*>(a.out + (size_t)t * a.H + h) = ov;
+}
+
+__global__ void __launch_bounds__(256) rms_norm_kernel(const uint16_t* __restrict__ x,
+                                                       const uint16_t* __restrict__ w, float eps,
+                                                       int64_t rows, int dim, uint16_t* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const uint16_t* xr = x + (size_t)r * dim;
+  const int nchunks = dim >> 3;
+  float acc = 0.0f;
+  for (int c = lane; c < nchunks; c += 32) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + c * 8);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float lo = bf_lo(u[i]), hi = bf_hi(u[i]);
+      acc = __fmaf_rn(lo, lo, acc);
+      acc = __fmaf_rn(hi, hi, acc);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+  const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)dim), eps)));
+  for (int c = lane; c < nchunks; c += 32) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + c * 8);
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + c * 8);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint16_t lo = f2bf(__fmul_rn(rbf(__fmul_rn(bf_lo(u[i]), rr)), bf_lo(wu[i])));
+      const uint16_t hi = f2bf(__fmul_rn(rbf(__fmul_rn(bf_hi(u[i]), rr)), bf_hi(wu[i])));
+      o[i] = (uint32_t)lo | ((uint32_t)hi << 16);
+    }
+    *reinterpret_cast<uint4*>(out + (size_t)r * dim + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st) {
+  const int64_t n = (int64_t)a.T * (a.H >> 3);
+  if (n <= 0) return cudaSuccess;
+  combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, float eps, int64_t rows, int dim,
+                            uint16_t* out, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  rms_norm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(x, w, eps, rows, dim, out);
+  return cudaGetLastError();
+}
+
+}  // namespace moe

@@ -1,0 +1,69 @@
+// common.cuh — device helpers shared by the MoE kernels (sm_100a).
+//
+// Numerics contract: every bf16 result is produced by rounding an fp32 value to
+// nearest-even (f2bf), after each operation of the reference's bf16 graph. Every
+// floating-point operation whose bits must match the CPU oracle is written with an
+// explicit __f*_rn intrinsic so nvcc cannot contract or reorder it.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define MOE_DEV __device__ __forceinline__
+
+namespace moe {
+
+MOE_DEV float bf2f(uint16_t h) { return __uint_as_float(((uint32_t)h) << 16); }
+
+// Round-to-nearest-even fp32 -> bf16 bits (NaN kept quiet).
+MOE_DEV uint16_t f2bf(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+MOE_DEV float rbf(float f) { return bf2f(f2bf(f)); }
+
+// bf16 pair packed in a uint32 (low half = first element).
+MOE_DEV float bf_lo(uint32_t v) { return __uint_as_float(v << 16); }
+MOE_DEV float bf_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+// exp(x): Cody-Waite range reduction (W. J. Cody, W. Waite, "Software Manual for the
+// Elementary Functions", 1980) with ln2 split into a 12-bit-short high part and a low
+// part, then the degree-7 Taylor polynomial of exp(r) (coefficients 1/i!) in Horner
+// form, scaled by 2^n. x > 88 gives +inf and x < -87 gives 0 by definition. The
+// operation sequence is the one the CPU oracle evaluates, so both give the same bits.
+MOE_DEV float exp_canon(float x) {
+  if (x != x) return x;
+  if (x > 88.0f) return __int_as_float(0x7f800000);
+  if (x < -87.0f) return 0.0f;
+  const float t = __fmul_rn(x, 0x1.715476p+0f);
+  const float n = rintf(t);
+  float r = __fmaf_rn(-n, 0x1.62e4p-1f, x);
+  r = __fmaf_rn(-n, 0x1.0bfbe8p-15f, r);
+  float p = 0x1.a01a02p-13f;
+  p = __fmaf_rn(p, r, 0x1.6c16c2p-10f);
+  p = __fmaf_rn(p, r, 0x1.111112p-7f);
+  p = __fmaf_rn(p, r, 0x1.555556p-5f);
+  p = __fmaf_rn(p, r, 0x1.555556p-3f);
+  p = __fmaf_rn(p, r, 0x1.0p-1f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  const int ni = (int)n;
+  const float scale = __uint_as_float((uint32_t)(ni + 127) << 23);
+  return __fmul_rn(p, scale);
+}
+
+// sigmoid(x) = 1 / (1 + exp(-x)) with IEEE add and divide.
+MOE_DEV float sigmoid_canon(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_canon(-x))); }
+
+// h = bf16(bf16(g * bf16(sigmoid(g))) * u): the reference's
+// x_gate.multiply(x_gate.sigmoid()).multiply(x_up) with bf16 results per op.
+MOE_DEV uint16_t swiglu_bf16(float g, float u) {
+  const float sg = rbf(sigmoid_canon(g));
+  const float a = rbf(__fmul_rn(g, sg));
+  return f2bf(__fmul_rn(a, u));
+}
+
+}  // namespace moe

@@ -1,0 +1,94 @@
+// kernels.cuh — argument blocks and launchers of the MoE kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace moe {
+
+// Router logits: logits[T, n_rows] = x[T, K] . dequant(W)^T in the canonical order.
+// Rows 0..E-1 come from the router weight; row E (when n_rows == E + 1) is the
+// shared_expert_gate row.
+struct RouterArgs {
+  const uint16_t* x;
+  int T, K, E, n_rows, group_size;
+  const uint32_t* w;
+  const uint16_t* s;
+  const uint16_t* b;
+  const uint32_t* gate_w;
+  const uint16_t* gate_s;
+  const uint16_t* gate_b;
+  uint16_t* logits;
+};
+
+struct TopkArgs {
+  const uint16_t* logits;  // [T, n_rows]
+  int T, E, n_rows, k, scoring, norm_topk_prob;
+  const uint16_t* expert_bias;  // [E] or null
+  uint32_t* idx;                // [T, k]
+  uint16_t* weights;            // [T, k] bf16
+  uint16_t* gate_val;           // [T] bf16 = sigmoid(logits[:, E]) or null
+};
+
+// Stable grouping of P pair ids by expert id (key[p] < E).
+struct GroupArgs {
+  const uint32_t* key;  // [P]
+  int64_t P;
+  int E;
+  int seg;          // pairs per segment
+  int nseg;         // ceil(P / seg)
+  int32_t* hist;    // [nseg, E] scratch
+  int32_t* segbase; // [nseg, E] scratch
+  int32_t* offsets; // [E + 1]
+  int32_t* active;  // [E] experts with pairs, ascending
+  int32_t* n_active;
+  uint32_t* perm;   // [P] pos -> p
+  uint32_t* inv;    // [P] p -> pos, may be null
+};
+
+// Grouped quantized GEMV/GEMM over expert-grouped rows (tensor cores via mma.sync,
+// 4-bit weights dequantised in registers).
+struct QgemvArgs {
+  const uint16_t* x;    // activations, row stride K
+  int x_mode;           // 0: row = pos, 1: row = perm[pos] / x_repeat, 2: row = lhs[perm[pos]]
+  int x_repeat;
+  const uint32_t* lhs;
+  const uint32_t* perm;     // pos -> original index, null = identity
+  const int32_t* offsets;   // [E+1], null = one expert (0) owning rows [0, n_identity)
+  const int32_t* active;    // slot -> expert, null = slot is the expert id
+  const int32_t* n_active;  // number of valid slots (device), null = all
+  int n_identity;
+  const uint32_t* w0;       // [E, N, K/8]
+  const uint16_t* s0;       // [E, N, K/64]
+  const uint16_t* b0;
+  const uint32_t* w1;       // second matrix (up) for the gated form
+  const uint16_t* s1;
+  const uint16_t* b1;
+  int N, K;
+  uint16_t* out;            // [rows, N] bf16
+  int out_mode;             // 0: row = pos, 1: row = perm[pos]
+  int sc_offset;            // set by the launcher: byte offset of the scale table in smem
+};
+
+struct CombineArgs {
+  const uint16_t* y;        // [P, H] expert outputs in grouped order
+  const uint32_t* inv;      // [P] pair -> grouped row
+  const uint16_t* weights;  // [T, k] bf16
+  const uint16_t* shared;   // [T, H] shared expert output or null
+  const uint16_t* gate_val; // [T] bf16 shared gate or null
+  int T, k, H;
+  uint16_t* out;            // [T, H]
+};
+
+cudaError_t launch_router(const RouterArgs& a, cudaStream_t st);
+cudaError_t launch_topk(const TopkArgs& a, cudaStream_t st);
+cudaError_t launch_group(const GroupArgs& a, cudaStream_t st);
+// gated: out = swiglu(x.W0^T, x.W1^T); else out = x.W0^T. max_rows_per_expert bounds
+// the token chunk the kernel stages at once; slots = grid.y.
+cudaError_t launch_qgemv(const QgemvArgs& a, bool gated, int slots, int max_rows_per_expert,
+                         cudaStream_t st);
+cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st);
+cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, float eps, int64_t rows, int dim,
+                            uint16_t* out, cudaStream_t st);
+
+}  // namespace moe

@@ -1,0 +1,261 @@
+// router.cu — R1..R4 of the MoE block: router logits, scoring, top-k, combine weights.
+//
+// Router logits must be bit-identical to the CPU oracle (the expert index sets are
+// compared bit for bit), so the router GEMV runs on CUDA cores in the canonical fp32
+// order: lane l of a warp owns the 32-element chunks c = l, l+32, ... of K and
+// accumulates acc = fma(x[e], w[e], acc) over each chunk in element order, with
+// w[e] = fma(scale, q, bias); the 32 lane sums are combined by the xor butterfly
+// (offsets 16, 8, 4, 2, 1) and lane 0 holds the result. One warp evaluates NE rows
+// against NT tokens at once (independent accumulators, same order for each).
+//
+// Reference: Linear::forward -> quantized_matmul (crates/mlx-nn/src/linear.rs:117-128),
+// softmax (qwen3_moe_python_port.rs:437), argpartition + slice + take_along_axis
+// (:438-441), norm_topk_prob (:442-445); LFM2 expert_bias + softmax
+// (lfm2_moe_python_port.rs:559-586, 680-686).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace moe {
+
+template <int NE, int NT>
+__global__ void __launch_bounds__(128) router_logits_kernel(RouterArgs a) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int row0 = (blockIdx.x * 4 + warp) * NE;
+  const int t0 = blockIdx.y * NT;
+  if (row0 >= a.n_rows) return;
+  const int nchunks = a.K >> 5;
+  const int wpr = a.K >> 3;
+  const int gpr = a.K / a.group_size;
+
+  float acc[NE][NT];
+#pragma unroll
+  for (int e = 0; e < NE; ++e)
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[e][t] = 0.0f;
+
+  const uint32_t* wrow[NE];
+  const uint16_t* srow[NE];
+  const uint16_t* brow[NE];
+  bool rvalid[NE];
+#pragma unroll
+  for (int e = 0; e < NE; ++e) {
+    const int r = row0 + e;
+    rvalid[e] = r < a.n_rows;
+    const bool is_gate = r >= a.E;  // the extra row is shared_expert_gate
+    const int rr = is_gate ? 0 : r;
+    wrow[e] = (is_gate ? a.gate_w : a.w) + (size_t)rr * wpr;
+    srow[e] = (is_gate ? a.gate_s : a.s) + (size_t)rr * gpr;
+    const uint16_t* bb = is_gate ? a.gate_b : a.b;
+    brow[e] = bb ? bb + (size_t)rr * gpr : nullptr;
+  }
+
+  for (int c = lane; c < nchunks; c += 32) {
+    const int g = (c * 32) / a.group_size;
+    uint4 wv[NE];
+    float sc[NE], bi[NE];
+#pragma unroll
+    for (int e = 0; e < NE; ++e) {
+      if (rvalid[e]) {
+        wv[e] = __ldg(reinterpret_cast<const uint4*>(wrow[e] + (size_t)c * 4));
+        sc[e] = bf2f(__ldg(srow[e] + g));
+        bi[e] = brow[e] ? bf2f(__ldg(brow[e] + g)) : 0.0f;
+      } else {
+        wv[e] = make_uint4(0, 0, 0, 0);
+        sc[e] = 0.0f;
+        bi[e] = 0.0f;
+      }
+    }
+#pragma unroll
+    for (int word = 0; word < 4; ++word) {
+      uint4 xv[NT];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        const int tok = t0 + t;
+        xv[t] = tok < a.T ? __ldg(reinterpret_cast<const uint4*>(a.x + (size_t)tok * a.K + c * 32 + word * 8))
+                          : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int el = 0; el < 8; ++el) {
+        float wq[NE];
+#pragma unroll
+        for (int e = 0; e < NE; ++e) {
+          const uint32_t wd = word == 0 ? wv[e].x : word == 1 ? wv[e].y : word == 2 ? wv[e].z : wv[e].w;
+          const float q = (float)((wd >> (4 * el)) & 0xfu);
+          wq[e] = __fmaf_rn(sc[e], q, bi[e]);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const uint32_t xw = (el >> 1) == 0 ? xv[t].x : (el >> 1) == 1 ? xv[t].y : (el >> 1) == 2 ? xv[t].z : xv[t].w;
+          const float xe = (el & 1) ? bf_hi(xw) : bf_lo(xw);
+#pragma unroll
+          for (int e = 0; e < NE; ++e) acc[e][t] = __fmaf_rn(xe, wq[e], acc[e][t]);
+        }
+      }
+    }
+  }
+
+#pragma unroll
+  for (int e = 0; e < NE; ++e)
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      float v = acc[e][t];
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+      acc[e][t] = v;
+    }
+  if (lane == 0) {
+#pragma unroll
+    for (int e = 0; e < NE; ++e)
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        const int tok = t0 + t;
+        if (rvalid[e] && tok < a.T) a.logits[(size_t)tok * a.n_rows + row0 + e] = f2bf(acc[e][t]);
+      }
+  }
+}
+
+// (key desc, index asc): true if (ka, ia) ranks before (kb, ib). Index 0x7fffffff
+// marks "no candidate".
+MOE_DEV bool ranks_before(float ka, int ia, float kb, int ib) {
+  if (ib == 0x7fffffff) return ia != 0x7fffffff;
+  if (ia == 0x7fffffff) return false;
+  return ka > kb || (ka == kb && ia < ib);
+}
+
+// One warp per token. Lane l holds experts l, l+32, ..., l+32*(PL-1).
+template <int PL>
+__global__ void __launch_bounds__(128) topk_kernel(TopkArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (t >= a.T) return;
+  const uint16_t* lrow = a.logits + (size_t)t * a.n_rows;
+
+  float val[PL], key[PL];
+  float l[PL];
+  float m = -__int_as_float(0x7f800000);
+#pragma unroll
+  for (int i = 0; i < PL; ++i) {
+    const int e = lane + 32 * i;
+    l[i] = 0.0f;
+    if (e < a.E) {
+      float v = bf2f(lrow[e]);
+      if (a.scoring == 1) v = rbf(__fadd_rn(v, bf2f(a.expert_bias[e])));
+      l[i] = v;
+      m = fmaxf(m, v);
+    }
+  }
+  if (a.scoring == 2) {
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      const int e = lane + 32 * i;
+      val[i] = 0.0f;
+      key[i] = 0.0f;
+      if (e < a.E) {
+        val[i] = rbf(sigmoid_canon(l[i]));
+        key[i] = rbf(__fadd_rn(val[i], bf2f(a.expert_bias[e])));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    float ex[PL];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      const int e = lane + 32 * i;
+      ex[i] = 0.0f;
+      if (e < a.E) {
+        ex[i] = exp_canon(__fsub_rn(l[i], m));
+        s = __fadd_rn(s, ex[i]);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      val[i] = rbf(__fdiv_rn(ex[i], s));
+      key[i] = val[i];
+    }
+  }
+
+  // k rounds of warp arg-max over the untaken candidates.
+  uint32_t taken = 0;
+  int my_sel = 0;
+  float my_w = 0.0f;
+  for (int j = 0; j < a.k; ++j) {
+    float bk = 0.0f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      const int e = lane + 32 * i;
+      if (e < a.E && !((taken >> i) & 1u) && ranks_before(key[i], e, bk, bi)) {
+        bk = key[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      const float ok = __shfl_xor_sync(0xffffffffu, bk, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (ranks_before(ok, oi, bk, bi)) {
+        bk = ok;
+        bi = oi;
+      }
+    }
+    // The owner marks the winner taken and broadcasts its weight value.
+    float wv = 0.0f;
+    if ((bi & 31) == lane) {
+#pragma unroll
+      for (int i = 0; i < PL; ++i)
+        if (i == (bi >> 5)) {
+          taken |= 1u << i;
+          wv = val[i];
+        }
+    }
+    wv = __shfl_sync(0xffffffffu, wv, bi & 31);
+    if (lane == j) {
+      my_sel = bi;
+      my_w = wv;
+    }
+  }
+  if (a.norm_topk_prob) {
+    float d = 0.0f;
+    for (int j = 0; j < a.k; ++j) d = __fadd_rn(d, __shfl_sync(0xffffffffu, my_w, j));
+    d = rbf(d);
+    my_w = rbf(__fdiv_rn(my_w, d));
+  }
+  if (lane < a.k) {
+    a.idx[(size_t)t * a.k + lane] = (uint32_t)my_sel;
+    a.weights[(size_t)t * a.k + lane] = f2bf(my_w);
+  }
+  if (a.gate_val && lane == 0) a.gate_val[t] = f2bf(sigmoid_canon(bf2f(lrow[a.E])));
+}
+
+cudaError_t launch_router(const RouterArgs& a, cudaStream_t st) {
+  if (a.T <= 0) return cudaSuccess;
+  if (a.T <= 4) {
+    dim3 grid((a.n_rows + 3) / 4, a.T);
+    router_logits_kernel<1, 1><<<grid, 128, 0, st>>>(a);
+  } else if (a.T <= 64) {
+    dim3 grid((a.n_rows + 7) / 8, (a.T + 3) / 4);
+    router_logits_kernel<2, 4><<<grid, 128, 0, st>>>(a);
+  } else {
+    dim3 grid((a.n_rows + 15) / 16, (a.T + 7) / 8);
+    router_logits_kernel<4, 8><<<grid, 128, 0, st>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_topk(const TopkArgs& a, cudaStream_t st) {
+  if (a.T <= 0) return cudaSuccess;
+  const int blocks = (a.T + 3) / 4;
+  const int pl = (a.E + 31) / 32;
+  if (pl <= 1) topk_kernel<1><<<blocks, 128, 0, st>>>(a);
+  else if (pl <= 2) topk_kernel<2><<<blocks, 128, 0, st>>>(a);
+  else if (pl <= 4) topk_kernel<4><<<blocks, 128, 0, st>>>(a);
+  else if (pl <= 8) topk_kernel<8><<<blocks, 128, 0, st>>>(a);
+  else topk_kernel<16><<<blocks, 128, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace moe
