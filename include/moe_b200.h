@@ -173,6 +173,17 @@ int moe_block_route(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_w
                     const void* x, int64_t T, uint32_t* idx, void* weights, int32_t* offsets,
                     uint32_t* perm);
 
+/*
+ * moe_block_forward with CUDA events between its stages; blocks until the block has
+ * run. stage_ms[8] receives the device time of: router, top-k, grouping, gate/up,
+ * down, shared gate/up, shared down, combine; n_active (optional) the number of
+ * distinct experts the routing selected. Replaces the per-stage timers of
+ * MoeProfileStats (qwen3_moe_python_port.rs:53-158, lfm2_moe_python_port.rs trace
+ * stats), which time graph construction on the host rather than device work.
+ */
+int moe_block_profile(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts,
+                      const void* x, int64_t T, void* out, float* stage_ms, int32_t* n_active);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,19 @@
+"""B200 (sm_100a) implementation of the mlx-rs device-side MoE / SwitchGLU block.
+
+Host-side mirror of the reference's Rust interface for this path:
+  ops.quantized_matmul / ops.gather_qmm / ops.fast_rms_norm
+      <- Array::quantized_matmul / Array::gather_qmm / Array::fast_rms_norm
+         (crates/mlx-core/src/ops.rs:592-637, 830-891, 691-701)
+  block.SparseMoeBlock, block.MoeFeedForward, block.RmsNorm, block.MoeStack
+      <- SparseMoeBlock::forward (qwen3_moe_python_port.rs:420-488),
+         MoeFeedForward::forward (lfm2_moe_python_port.rs:541-740),
+         RmsNorm::forward (crates/mlx-nn/src/rms_norm.rs:30-34)
+Every call goes through the C ABI of libmoe_b200.so (include/moe_b200.h); there is no
+other compute path. torch supplies device memory and streams only.
+"""
+from ._lib import MlxError, library, library_path  # noqa: F401
+from . import ops  # noqa: F401
+from . import block  # noqa: F401
+from . import synth  # noqa: F401
+
+__all__ = ["MlxError", "library", "library_path", "ops", "block", "synth"]

@@ -184,9 +184,17 @@ int check_block(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights
   return MOE_OK;
 }
 
+// Stage boundaries recorded by moe_block_profile (ev == null: not recorded).
+enum Stage { kRouter = 0, kTopk, kGroup, kGateUp, kDown, kSharedGateUp, kSharedDown, kCombine, kStages };
+
+#define MOE_MARK(ev, i, st) \
+  do {                        \
+    if (ev) MOE_CUDA(ctx, cudaEventRecord((ev)[i], st)); \
+  } while (0)
+
 // Routing + grouping of one block call into ws.
 int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* w, const void* x, int64_t T,
-              const BlockWs& ws) {
+              const BlockWs& ws, cudaEvent_t* ev = nullptr) {
   const int E = c->num_experts;
   const bool gate_row = c->shared_inter > 0 && c->has_shared_gate;
   moe::RouterArgs ra{};
@@ -203,6 +211,7 @@ int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* 
   ra.gate_s = static_cast<const uint16_t*>(w->shared_expert_gate.scales);
   ra.gate_b = static_cast<const uint16_t*>(w->shared_expert_gate.biases);
   ra.logits = ws.logits;
+  MOE_MARK(ev, kRouter, ctx->stream);
   MOE_CUDA(ctx, moe::launch_router(ra, ctx->stream));
 
   moe::TopkArgs ta{};
@@ -217,6 +226,7 @@ int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* 
   ta.idx = ws.idx;
   ta.weights = ws.wsel;
   ta.gate_val = gate_row ? ws.gate_val : nullptr;
+  MOE_MARK(ev, kTopk, ctx->stream);
   MOE_CUDA(ctx, moe::launch_topk(ta, ctx->stream));
 
   moe::GroupArgs ga{};
@@ -232,6 +242,7 @@ int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* 
   ga.n_active = ws.n_active;
   ga.perm = ws.perm;
   ga.inv = ws.inv;
+  MOE_MARK(ev, kGroup, ctx->stream);
   MOE_CUDA(ctx, moe::launch_group(ga, ctx->stream));
   return MOE_OK;
 }
@@ -249,6 +260,100 @@ moe::QgemvArgs qgemv_args(const moe_qweight& m0, const moe_qweight* m1, int N, i
   q.N = N;
   q.K = K;
   return q;
+}
+
+}  // namespace
+
+namespace {
+
+int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x, int64_t T,
+              void* out, cudaEvent_t* ev) {
+  if (!ctx) return MOE_ERR_INVALID;
+  ctx->last_error.clear();
+  const char* fn = "moe_block_forward";
+  int rc = check_block(ctx, cfg, wts, fn);
+  if (rc) return rc;
+  if (T < 0 || T > (INT32_MAX / 64)) return fail(ctx, MOE_ERR_INVALID, "%s: bad T", fn);
+  if (T == 0) return MOE_OK;
+  if (!x || !out || !aligned16(x) || !aligned16(out))
+    return fail(ctx, MOE_ERR_INVALID, "%s: x and out must be non-null and 16-byte aligned", fn);
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  rc = ensure_scratch(ctx, carve_block(nullptr, cfg, T).bytes);
+  if (rc) return rc;
+  BlockWs ws = carve_block(ctx->scratch, cfg, T);
+  rc = run_route(ctx, cfg, wts, x, T, ws, ev);
+  if (rc) return rc;
+
+  const int E = cfg->num_experts, H = cfg->hidden, I = cfg->moe_inter, k = cfg->top_k;
+  const int64_t P = T * k;
+  const int slots = (int)std::min<int64_t>(P, E);
+  const int max_rows = (int)std::min<int64_t>(T, 16);
+
+  // SwitchGLU gate/up + SiLU*up over grouped rows (x row = pair / k).
+  moe::QgemvArgs gu = qgemv_args(wts->gate, &wts->up, I, H);
+  gu.x = static_cast<const uint16_t*>(x);
+  gu.x_mode = 1;
+  gu.x_repeat = k;
+  gu.perm = ws.perm;
+  gu.offsets = ws.offsets;
+  gu.active = ws.active;
+  gu.n_active = ws.n_active;
+  gu.out = ws.hbuf;
+  gu.out_mode = 0;
+  MOE_MARK(ev, kGateUp, ctx->stream);
+  MOE_CUDA(ctx, moe::launch_qgemv(gu, true, slots, max_rows, ctx->stream));
+
+  // down projection over the same grouped rows.
+  moe::QgemvArgs dn = qgemv_args(wts->down, nullptr, H, I);
+  dn.x = ws.hbuf;
+  dn.x_mode = 0;
+  dn.perm = ws.perm;
+  dn.offsets = ws.offsets;
+  dn.active = ws.active;
+  dn.n_active = ws.n_active;
+  dn.out = ws.ybuf;
+  dn.out_mode = 0;
+  MOE_MARK(ev, kDown, ctx->stream);
+  MOE_CUDA(ctx, moe::launch_qgemv(dn, false, slots, max_rows, ctx->stream));
+
+  const bool shared = cfg->shared_inter > 0;
+  if (!shared) {
+    MOE_MARK(ev, kSharedGateUp, ctx->stream);
+    MOE_MARK(ev, kSharedDown, ctx->stream);
+  }
+  if (shared) {
+    const int Is = cfg->shared_inter;
+    moe::QgemvArgs sgu = qgemv_args(wts->shared_gate, &wts->shared_up, Is, H);
+    sgu.x = static_cast<const uint16_t*>(x);
+    sgu.x_mode = 0;
+    sgu.n_identity = (int)T;
+    sgu.out = ws.hs;
+    MOE_MARK(ev, kSharedGateUp, ctx->stream);
+    MOE_CUDA(ctx, moe::launch_qgemv(sgu, true, 1, max_rows, ctx->stream));
+    moe::QgemvArgs sdn = qgemv_args(wts->shared_down, nullptr, H, Is);
+    sdn.x = ws.hs;
+    sdn.x_mode = 0;
+    sdn.n_identity = (int)T;
+    sdn.out = ws.ys;
+    MOE_MARK(ev, kSharedDown, ctx->stream);
+    MOE_CUDA(ctx, moe::launch_qgemv(sdn, false, 1, max_rows, ctx->stream));
+  }
+
+  moe::CombineArgs ca{};
+  ca.y = ws.ybuf;
+  ca.inv = ws.inv;
+  ca.weights = ws.wsel;
+  ca.shared = shared ? ws.ys : nullptr;
+  ca.gate_val = (shared && cfg->has_shared_gate) ? ws.gate_val : nullptr;
+  ca.T = (int)T;
+  ca.k = k;
+  ca.H = H;
+  ca.out = static_cast<uint16_t*>(out);
+  MOE_MARK(ev, kCombine, ctx->stream);
+  MOE_CUDA(ctx, moe::launch_combine(ca, ctx->stream));
+  MOE_MARK(ev, kStages, ctx->stream);
+  return MOE_OK;
 }
 
 }  // namespace
@@ -430,82 +535,33 @@ int moe_block_route(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_w
 
 int moe_block_forward(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x,
                       int64_t T, void* out) {
+  return run_block(ctx, cfg, wts, x, T, out, nullptr);
+}
+
+int moe_block_profile(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x,
+                      int64_t T, void* out, float* stage_ms, int32_t* n_active) {
   if (!ctx) return MOE_ERR_INVALID;
-  ctx->last_error.clear();
-  const char* fn = "moe_block_forward";
-  int rc = check_block(ctx, cfg, wts, fn);
-  if (rc) return rc;
-  if (T < 0 || T > (INT32_MAX / 64)) return fail(ctx, MOE_ERR_INVALID, "%s: bad T", fn);
-  if (T == 0) return MOE_OK;
-  if (!x || !out || !aligned16(x) || !aligned16(out))
-    return fail(ctx, MOE_ERR_INVALID, "%s: x and out must be non-null and 16-byte aligned", fn);
+  if (!stage_ms) return fail(ctx, MOE_ERR_INVALID, "moe_block_profile: stage_ms is null");
   DeviceGuard g(ctx->device);
   if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
-  rc = ensure_scratch(ctx, carve_block(nullptr, cfg, T).bytes);
-  if (rc) return rc;
-  BlockWs ws = carve_block(ctx->scratch, cfg, T);
-  rc = run_route(ctx, cfg, wts, x, T, ws);
-  if (rc) return rc;
-
-  const int E = cfg->num_experts, H = cfg->hidden, I = cfg->moe_inter, k = cfg->top_k;
-  const int64_t P = T * k;
-  const int slots = (int)std::min<int64_t>(P, E);
-  const int max_rows = (int)std::min<int64_t>(T, 16);
-
-  // SwitchGLU gate/up + SiLU*up over grouped rows (x row = pair / k).
-  moe::QgemvArgs gu = qgemv_args(wts->gate, &wts->up, I, H);
-  gu.x = static_cast<const uint16_t*>(x);
-  gu.x_mode = 1;
-  gu.x_repeat = k;
-  gu.perm = ws.perm;
-  gu.offsets = ws.offsets;
-  gu.active = ws.active;
-  gu.n_active = ws.n_active;
-  gu.out = ws.hbuf;
-  gu.out_mode = 0;
-  MOE_CUDA(ctx, moe::launch_qgemv(gu, true, slots, max_rows, ctx->stream));
-
-  // down projection over the same grouped rows.
-  moe::QgemvArgs dn = qgemv_args(wts->down, nullptr, H, I);
-  dn.x = ws.hbuf;
-  dn.x_mode = 0;
-  dn.perm = ws.perm;
-  dn.offsets = ws.offsets;
-  dn.active = ws.active;
-  dn.n_active = ws.n_active;
-  dn.out = ws.ybuf;
-  dn.out_mode = 0;
-  MOE_CUDA(ctx, moe::launch_qgemv(dn, false, slots, max_rows, ctx->stream));
-
-  const bool shared = cfg->shared_inter > 0;
-  if (shared) {
-    const int Is = cfg->shared_inter;
-    moe::QgemvArgs sgu = qgemv_args(wts->shared_gate, &wts->shared_up, Is, H);
-    sgu.x = static_cast<const uint16_t*>(x);
-    sgu.x_mode = 0;
-    sgu.n_identity = (int)T;
-    sgu.out = ws.hs;
-    MOE_CUDA(ctx, moe::launch_qgemv(sgu, true, 1, max_rows, ctx->stream));
-    moe::QgemvArgs sdn = qgemv_args(wts->shared_down, nullptr, H, Is);
-    sdn.x = ws.hs;
-    sdn.x_mode = 0;
-    sdn.n_identity = (int)T;
-    sdn.out = ws.ys;
-    MOE_CUDA(ctx, moe::launch_qgemv(sdn, false, 1, max_rows, ctx->stream));
+  cudaEvent_t ev[kStages + 1] = {};
+  for (int i = 0; i <= kStages; ++i) MOE_CUDA(ctx, cudaEventCreate(&ev[i]));
+  int rc = run_block(ctx, cfg, wts, x, T, out, T > 0 ? ev : nullptr);
+  if (rc == MOE_OK && T > 0) {
+    cudaError_t e = cudaEventSynchronize(ev[kStages]);
+    for (int i = 0; i < kStages && e == cudaSuccess; ++i) e = cudaEventElapsedTime(&stage_ms[i], ev[i], ev[i + 1]);
+    if (e != cudaSuccess) rc = fail(ctx, MOE_ERR_CUDA, "moe_block_profile: %s", cudaGetErrorString(e));
+    if (rc == MOE_OK && n_active) {
+      BlockWs ws = carve_block(ctx->scratch, cfg, T);
+      e = cudaMemcpy(n_active, ws.n_active, sizeof(int32_t), cudaMemcpyDeviceToHost);
+      if (e != cudaSuccess) rc = fail(ctx, MOE_ERR_CUDA, "moe_block_profile: %s", cudaGetErrorString(e));
+    }
+  } else if (rc == MOE_OK) {
+    for (int i = 0; i < kStages; ++i) stage_ms[i] = 0.0f;
+    if (n_active) *n_active = 0;
   }
-
-  moe::CombineArgs ca{};
-  ca.y = ws.ybuf;
-  ca.inv = ws.inv;
-  ca.weights = ws.wsel;
-  ca.shared = shared ? ws.ys : nullptr;
-  ca.gate_val = (shared && cfg->has_shared_gate) ? ws.gate_val : nullptr;
-  ca.T = (int)T;
-  ca.k = k;
-  ca.H = H;
-  ca.out = static_cast<uint16_t*>(out);
-  MOE_CUDA(ctx, moe::launch_combine(ca, ctx->stream));
-  return MOE_OK;
+  for (int i = 0; i <= kStages; ++i) cudaEventDestroy(ev[i]);
+  return rc;
 }
 
 }  // extern "C"

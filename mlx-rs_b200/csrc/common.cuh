@@ -40,7 +40,7 @@ MOE_DEV float exp_canon(float x) {
   if (x < -87.0f) return 0.0f;
   const float t = __fmul_rn(x, 0x1.715476p+0f);
   const float n = rintf(t);
-  float r = __fmaf_rn(-n, 0x1.62e4p-1f, x);
+  float r = __fmaf_rn(-n, 0x1.62ep-1f, x);
   r = __fmaf_rn(-n, 0x1.0bfbe8p-15f, r);
   float p = 0x1.a01a02p-13f;
   p = __fmaf_rn(p, r, 0x1.6c16c2p-10f);

@@ -313,8 +313,17 @@ static cudaError_t launch_qgemv_t(const QgemvArgs& a, int slots, cudaStream_t st
   const size_t smem = front + sizeof(float2) * TL::kScRows * G;
   if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
   auto kern = qgemv_kernel<GATED, NT8>;
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (err != cudaSuccess) return err;
+  // Raise the dynamic shared memory limit once per device and size (not per launch).
+  static thread_local int set_dev = -1;
+  static thread_local size_t set_smem = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != set_dev || smem > set_smem) {
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (err != cudaSuccess) return err;
+    set_dev = dev;
+    set_smem = 227 * 1024;
+  }
   dim3 grid((a.N + TL::kRows - 1) / TL::kRows, slots);
   QgemvArgs b = a;
   b.sc_offset = (int)front;

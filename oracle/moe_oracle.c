@@ -130,7 +130,7 @@ uint16_t oracle_f32_to_bf16(float x) { return f2bf(x); }
  * sequence of IEEE operations, so both produce identical bits.
  */
 #define OR_LOG2E 0x1.715476p+0f
-#define OR_LN2_HI 0x1.62e4p-1f /* 0.693115234375 */
+#define OR_LN2_HI 0x1.62ep-1f /* 0.693115234375 */
 #define OR_LN2_LO 0x1.0bfbe8p-15f
 #define OR_C2 0x1.0p-1f
 #define OR_C3 0x1.555556p-3f
@@ -460,6 +460,12 @@ static void topk_row(const uint16_t* key, int64_t E, int k, uint32_t* sel) {
         }
         sel[j] = (uint32_t)best;
     }
+}
+
+int oracle_topk_rows(const uint16_t* keys, int64_t rows, int64_t E, int k, uint32_t* idx) {
+    if (k <= 0 || k > E) return -6;
+    for (int64_t r = 0; r < rows; ++r) topk_row(keys + r * E, E, k, idx + r * k);
+    return 0;
 }
 
 /*

@@ -92,6 +92,9 @@ int oracle_gather_qmm(const uint16_t* x, int64_t K, int64_t x_repeat, const uint
 
 int oracle_softmax_rows(const uint16_t* logits, int64_t rows, int64_t n, uint16_t* probs);
 
+/* Top-k of each row of bf16 keys by (key desc, index asc). */
+int oracle_topk_rows(const uint16_t* keys, int64_t rows, int64_t E, int k, uint32_t* idx);
+
 int oracle_route(const oracle_block_config* cfg, const oracle_block_weights* wt,
                  const uint16_t* x, int64_t T, uint32_t* idx, uint16_t* weights,
                  uint16_t* logits_out, uint16_t* scores_out, int nthreads);

@@ -68,6 +68,7 @@ def lib():
                                         C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p,
                                         C.c_int64, C.c_int, C.c_int, C.c_void_p, C.c_int]
         L.oracle_softmax_rows.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p]
+        L.oracle_topk_rows.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_int, C.c_void_p]
         L.oracle_route.argtypes = [C.POINTER(_Cfg), C.POINTER(_Wts), C.c_void_p, C.c_int64,
                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
         L.oracle_group_by_expert.argtypes = [C.c_int64, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
@@ -143,6 +144,14 @@ def softmax_rows(logits):
     _check(lib().oracle_softmax_rows(_p(logits), logits.shape[0], logits.shape[1], _p(out)),
            "oracle_softmax_rows")
     return out
+
+
+def topk_rows(keys, k):
+    keys = _c(keys, np.uint16)
+    rows, E = keys.shape
+    idx = np.empty((rows, k), np.uint32)
+    _check(lib().oracle_topk_rows(_p(keys), rows, E, k, _p(idx)), "oracle_topk_rows")
+    return idx
 
 
 def rms_norm(x, w, eps, nthreads=0):
