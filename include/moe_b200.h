@@ -184,6 +184,30 @@ int moe_block_route(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_w
 int moe_block_profile(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts,
                       const void* x, int64_t T, void* out, float* stage_ms, int32_t* n_active);
 
+/*
+ * moe_gather_qmm without any device allocation. Same arguments, semantics and results
+ * as moe_gather_qmm; no counterpart in the reference (mlx-c allocates through MLX's own
+ * allocator). For callers that cannot let a library allocate GPU memory: a host
+ * framework whose allocator already owns the device memory, or a latency-critical
+ * loop where cudaMalloc/cudaFree (which may synchronise the device) are not allowed.
+ * Its row-grouping scratch is a fixed 64 KiB array in the library's device image
+ * (held by every GPU that loads the library until the process exits), so
+ * batch <= MOE_NOALLOC_MAX_BATCH and num_experts <= MOE_NOALLOC_MAX_EXPERTS; larger
+ * calls return MOE_ERR_INVALID. The context provides the device, the stream and the
+ * error message; its own scratch is not used. All calls on a device share the array:
+ * calls that overlap on the GPU race, so order them. The first call on each device
+ * looks up the array's device address (with that device current); make it before any
+ * stream capture.
+ */
+#define MOE_NOALLOC_MAX_BATCH 4096
+#define MOE_NOALLOC_MAX_EXPERTS 512
+int moe_gather_qmm_noalloc(moe_ctx* ctx, const void* x, int64_t x_rows, int64_t K,
+                           int64_t x_repeat, const uint32_t* lhs_indices, const uint32_t* w,
+                           const void* scales, const void* biases, int64_t num_experts,
+                           int64_t N, const uint32_t* rhs_indices, int64_t batch,
+                           int transpose, int group_size, int bits, int sorted_indices,
+                           void* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -72,6 +72,10 @@ SIGNATURES = {
                                  C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64,
                                  C.c_int64, C.c_void_p, C.c_int64, C.c_int, C.c_int, C.c_int,
                                  C.c_int, C.c_void_p]),
+    "moe_gather_qmm_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
+                                         C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64,
+                                         C.c_int64, C.c_void_p, C.c_int64, C.c_int, C.c_int, C.c_int,
+                                         C.c_int, C.c_void_p]),
     "moe_fast_rms_norm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_int64,
                                     C.c_int64, C.c_void_p]),
     "moe_block_forward": (C.c_int, [C.c_void_p, C.POINTER(BlockConfig), C.POINTER(BlockWeights),

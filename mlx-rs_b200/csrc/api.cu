@@ -565,3 +565,11 @@ int moe_block_profile(moe_ctx* ctx, const moe_block_config* cfg, const moe_block
 }
 
 }  // extern "C"
+
+// Accessors for moe_gather_qmm_noalloc (api_noalloc.cu), which must not reach the
+// context's scratch.
+namespace moe_internal {
+int ctx_device(const moe_ctx* ctx) { return ctx->device; }
+void* ctx_stream(const moe_ctx* ctx) { return ctx->stream; }
+void ctx_set_error(moe_ctx* ctx, const char* msg) { ctx->last_error = msg; }
+}  // namespace moe_internal
