@@ -82,6 +82,16 @@ class ClockSampler:
         except Exception:
             self.proc = None
 
+    def wait_first_sample(self, timeout=3.0):
+        t_end = time.time() + timeout
+        while self.proc and time.time() < t_end:
+            try:
+                if os.path.getsize(self.path) > 0:
+                    return
+            except OSError:
+                pass
+            time.sleep(0.05)
+
     def stop(self):
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
@@ -251,13 +261,29 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    # nvidia-smi samples every 200 ms, longer than the timed steps take, so the sampler
+    # runs across a window of back-to-back (untimed) steps that brackets the timed ones.
     clocks = ClockSampler(local)
     clocks.start()
+    clocks.wait_first_sample()
+    t_busy = time.perf_counter() + 0.6
+    while time.perf_counter() < t_busy:
+        for i in range(8):
+            step(i)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
     evs = [step(i) for i in range(args.steps)]
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    t_busy = time.perf_counter() + 0.6
+    while time.perf_counter() < t_busy:
+        for i in range(8):
+            step(i)
+        torch.cuda.synchronize()
     clock_info = clocks.stop()
     step_ms = [a.elapsed_time(b) for a, b in evs]
     ms = statistics.mean(step_ms)
@@ -347,6 +373,7 @@ def main():
                        "seq_len": 1, "parallelism": f"replicas{world}" if world > 1 else "single",
                        "experts": cfg.num_experts, "top_k": cfg.top_k, "hidden": H, "moe_inter": cfg.moe_inter,
                        "l2": "flushed (256 MiB write) before every timed step", "launch": mode,
+                       "clock_window": "nvidia-smi every 200 ms across 0.6 s of untimed steps, the timed steps, 0.6 s more",
                        "distinct_experts_per_step": U, "sweep_eager": sweep},
             "roofline": {"bound": "hbm", "kernel": f"qgemv {dom}", "achieved": achieved, "peak": hbm,
                          "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind,

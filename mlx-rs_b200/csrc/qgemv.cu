@@ -78,10 +78,17 @@ struct RowMap {
 // Shared memory: [xs: TOK rows x (2K + 16) bytes][xsum: TOK x G floats], padded to at
 // least the cross-warp reduction buffer (which reuses it after the K loop), then
 // [sc: kScRows x G float2] at a.sc_offset (kept across token chunks).
+//
+// Memory-level parallelism: each warp owns a contiguous run of K groups and keeps a ring
+// of kPF groups of weight loads in flight (kPF x 4 m16 tiles x 2 rows x 8 bytes per
+// lane); the loads for the first kPF groups are issued before the shared-memory staging
+// of scales and activations, so their latency overlaps it.
 template <bool GATED, int NT8>
-__global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a) {
+__global__ void __launch_bounds__(128, 2) qgemv_kernel(QgemvArgs a) {
   using TL = Tile<GATED>;
   constexpr int TOK = 8 * NT8;
+  constexpr int kPF = 4;
+  constexpr int MT = TL::kMTiles;
   extern __shared__ __align__(16) unsigned char smem[];
   const int K = a.K, N = a.N;
   const int G = K >> 6;
@@ -103,31 +110,14 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a) {
   const int n0 = blockIdx.x * TL::kRows;
   const RowMap rm{a.x_mode, a.x_repeat, a.lhs, a.perm};
 
-  // ---- scales: sc[r][g] = (s, b - 128 s) for the CTA's rows
-  for (int idx = tid; idx < TL::kScRows * G; idx += 128) {
-    const int r = idx / G, g = idx - r * G;
-    const int mat = r / TL::kRows;
-    const int row = n0 + (r - mat * TL::kRows);
-    float s = 0.0f, cb = 0.0f;
-    if (row < N) {
-      const uint16_t* S = mat ? a.s1 : a.s0;
-      const uint16_t* B = mat ? a.b1 : a.b0;
-      const size_t off = ((size_t)e * N + row) * G + g;
-      s = bf2f(S[off]);
-      const float b = B ? bf2f(B[off]) : 0.0f;
-      cb = __fmaf_rn(-128.0f, s, b);
-    }
-    sc[r * G + g] = make_float2(s, cb);
-  }
-
   // ---- per-lane weight row pointers (rows gq and gq+8 of each m16 tile)
-  const uint32_t* wp_lo[TL::kMTiles];
-  const uint32_t* wp_hi[TL::kMTiles];
-  bool ok_lo[TL::kMTiles], ok_hi[TL::kMTiles];
-  int scr_lo[TL::kMTiles], scr_hi[TL::kMTiles];  // sc row index
+  const uint32_t* wp_lo[MT];
+  const uint32_t* wp_hi[MT];
+  bool ok_lo[MT], ok_hi[MT];
+  int scr_lo[MT], scr_hi[MT];  // sc row index
   const int wpr = K >> 3;
 #pragma unroll
-  for (int mt = 0; mt < TL::kMTiles; ++mt) {
+  for (int mt = 0; mt < MT; ++mt) {
     const int mat = GATED ? (mt >> 1) : 0;
     const int rloc = GATED ? (mt & 1) * 16 : mt * 16;
     const uint32_t* W = mat ? a.w1 : a.w0;
@@ -143,19 +133,73 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a) {
   const int g_begin = min(G, warp * gpw);
   const int g_end = min(G, g_begin + gpw);
 
+  uint2 wl[kPF][MT], wh[kPF][MT];
+  auto load_group = [&](int slotp, int g) {
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const bool go = g < g_end;
+      wl[slotp][mt] = (go && ok_lo[mt]) ? ldg_nc_u2(wp_lo[mt] + g * 8) : make_uint2(0, 0);
+      wh[slotp][mt] = (go && ok_hi[mt]) ? ldg_nc_u2(wp_hi[mt] + g * 8) : make_uint2(0, 0);
+    }
+  };
+
+  bool first_chunk = true;
   for (int64_t cbase = row_begin; cbase < row_end; cbase += TOK) {
     const int ntok = (row_end - cbase < TOK) ? (int)(row_end - cbase) : TOK;
+    // ---- issue the first kPF groups of weight loads
+#pragma unroll
+    for (int i = 0; i < kPF; ++i) load_group(i, g_begin + i);
     __syncthreads();  // previous chunk's readers of xs / the reduction buffer are done
-    // ---- stage the token chunk: permuted bf16 tile + per-group sums
-    const int units = TOK * G * 4;
-    for (int u0 = 0; u0 < units; u0 += 128) {  // uniform trip count: the shuffles below need all lanes
+    if (first_chunk) {
+      // ---- scales: sc[r][g] = (s, b - 128 s); 16-byte loads of 8 groups of one row
+      const int cpr = (G + 7) >> 3;  // 8-group chunks per row
+      for (int idx = tid; idx < TL::kScRows * cpr; idx += 128) {
+        const int r = idx / cpr, c8 = idx - r * cpr;
+        const int mat = r / TL::kRows;
+        const int row = n0 + (r - mat * TL::kRows);
+        const uint16_t* S = mat ? a.s1 : a.s0;
+        const uint16_t* B = mat ? a.b1 : a.b0;
+        const size_t off = ((size_t)e * N + (row < N ? row : 0)) * G + c8 * 8;
+        const int ng = min(8, G - c8 * 8);
+        uint16_t sv[8], bv[8];
+        if (ng == 8 && (off & 7) == 0) {
+          const uint4 s4 = *reinterpret_cast<const uint4*>(S + off);
+          const uint4 b4 = B ? *reinterpret_cast<const uint4*>(B + off) : make_uint4(0, 0, 0, 0);
+          const uint32_t su[4] = {s4.x, s4.y, s4.z, s4.w}, bu[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            sv[2 * i] = (uint16_t)(su[i] & 0xffff); sv[2 * i + 1] = (uint16_t)(su[i] >> 16);
+            bv[2 * i] = (uint16_t)(bu[i] & 0xffff); bv[2 * i + 1] = (uint16_t)(bu[i] >> 16);
+          }
+        } else {
+          for (int i = 0; i < 8; ++i) {
+            sv[i] = i < ng ? S[off + i] : 0;
+            bv[i] = (i < ng && B) ? B[off + i] : 0;
+          }
+        }
+        for (int i = 0; i < ng; ++i) {
+          float s = 0.0f, cb = 0.0f;
+          if (row < N) {
+            s = bf2f(sv[i]);
+            cb = __fmaf_rn(-128.0f, s, bf2f(bv[i]));
+          }
+          sc[r * G + c8 * 8 + i] = make_float2(s, cb);
+        }
+      }
+      first_chunk = false;
+    }
+    // ---- stage the valid token rows: permuted bf16 tile + per-group sums. Rows past
+    // ntok are not written: a column of the MMA result depends on its own token only,
+    // and those columns are never stored.
+    const int units = ntok * G * 4;
+    for (int u0 = 0; u0 < units; u0 += 128) {  // uniform trip count: the shuffles need all lanes
       const int u = u0 + tid;
       const bool uvalid = u < units;
       const int c = u & 3;
       const int g = (u >> 2) % G;
       const int t = (u >> 2) / G;
       uint32_t in[8];
-      if (uvalid && t < ntok) {
+      if (uvalid) {
         const int64_t xr = rm.xrow(cbase + t);
         const uint4* src = reinterpret_cast<const uint4*>(a.x + (size_t)xr * K + g * 64 + c * 16);
         const uint4 v0 = src[0], v1 = src[1];
@@ -188,74 +232,73 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a) {
     }
     __syncthreads();
 
-    // ---- main loop over this warp's groups
-    float acc[TL::kMTiles][NT8][4];
+    // ---- main loop over this warp's groups with a kPF-deep ring of weight loads
+    float acc[MT][NT8][4];
 #pragma unroll
-    for (int mt = 0; mt < TL::kMTiles; ++mt)
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
       for (int n = 0; n < NT8; ++n)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[mt][n][i] = 0.0f;
-
-    uint2 wlo[TL::kMTiles], whi[TL::kMTiles];
+    const bool n1_live = NT8 > 1 && ntok > 8;
+    for (int gb = g_begin; gb < g_end; gb += kPF) {
 #pragma unroll
-    for (int mt = 0; mt < TL::kMTiles; ++mt) {
-      const bool go = g_begin < g_end;
-      wlo[mt] = (go && ok_lo[mt]) ? ldg_nc_u2(wp_lo[mt] + g_begin * 8) : make_uint2(0, 0);
-      whi[mt] = (go && ok_hi[mt]) ? ldg_nc_u2(wp_hi[mt] + g_begin * 8) : make_uint2(0, 0);
-    }
-    for (int g = g_begin; g < g_end; ++g) {
-      // prefetch the next group's weights
-      uint2 nlo[TL::kMTiles], nhi[TL::kMTiles];
-      const bool more = g + 1 < g_end;
+      for (int i = 0; i < kPF; ++i) {
+        const int g = gb + i;
+        if (g < g_end) {
+          uint32_t bf[NT8][8];
+          float X0[NT8], X1[NT8];
 #pragma unroll
-      for (int mt = 0; mt < TL::kMTiles; ++mt) {
-        nlo[mt] = (more && ok_lo[mt]) ? ldg_nc_u2(wp_lo[mt] + (g + 1) * 8) : make_uint2(0, 0);
-        nhi[mt] = (more && ok_hi[mt]) ? ldg_nc_u2(wp_hi[mt] + (g + 1) * 8) : make_uint2(0, 0);
-      }
-      // activation fragments and group sums
-      uint32_t bf[NT8][8];
-      float X0[NT8], X1[NT8];
+          for (int n = 0; n < NT8; ++n) {
+            if (n == 0 || n1_live) {
+              const uint4* src =
+                  reinterpret_cast<const uint4*>(xs + (size_t)(n * 8 + gq) * xs_stride + g * 128 + cq * 32);
+              const uint4 v0 = src[0], v1 = src[1];
+              bf[n][0] = v0.x; bf[n][1] = v0.y; bf[n][2] = v0.z; bf[n][3] = v0.w;
+              bf[n][4] = v1.x; bf[n][5] = v1.y; bf[n][6] = v1.z; bf[n][7] = v1.w;
+              X0[n] = xsum[(n * 8 + 2 * cq) * G + g];
+              X1[n] = xsum[(n * 8 + 2 * cq + 1) * G + g];
+            }
+          }
 #pragma unroll
-      for (int n = 0; n < NT8; ++n) {
-        const uint4* src = reinterpret_cast<const uint4*>(xs + (size_t)(n * 8 + gq) * xs_stride + g * 128 + cq * 32);
-        const uint4 v0 = src[0], v1 = src[1];
-        bf[n][0] = v0.x; bf[n][1] = v0.y; bf[n][2] = v0.z; bf[n][3] = v0.w;
-        bf[n][4] = v1.x; bf[n][5] = v1.y; bf[n][6] = v1.z; bf[n][7] = v1.w;
-        X0[n] = xsum[(n * 8 + 2 * cq) * G + g];
-        X1[n] = xsum[(n * 8 + 2 * cq + 1) * G + g];
-      }
+          for (int mt = 0; mt < MT; ++mt) {
+            const float2 slo = sc[scr_lo[mt] * G + g];
+            const float2 shi = sc[scr_hi[mt] * G + g];
+            float d[NT8][4];
 #pragma unroll
-      for (int mt = 0; mt < TL::kMTiles; ++mt) {
-        const float2 slo = sc[scr_lo[mt] * G + g];
-        const float2 shi = sc[scr_hi[mt] * G + g];
+            for (int n = 0; n < NT8; ++n)
 #pragma unroll
-        for (int n = 0; n < NT8; ++n) {
-          float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+              for (int q = 0; q < 4; ++q) d[n][q] = 0.0f;
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            mma_bf16_16816(d, nib_pair(wlo[mt].x, j), nib_pair(whi[mt].x, j), nib_pair(wlo[mt].y, j),
-                           nib_pair(whi[mt].y, j), bf[n][2 * j], bf[n][2 * j + 1]);
-          acc[mt][n][0] = __fmaf_rn(slo.y, X0[n], __fmaf_rn(slo.x, d[0], acc[mt][n][0]));
-          acc[mt][n][1] = __fmaf_rn(slo.y, X1[n], __fmaf_rn(slo.x, d[1], acc[mt][n][1]));
-          acc[mt][n][2] = __fmaf_rn(shi.y, X0[n], __fmaf_rn(shi.x, d[2], acc[mt][n][2]));
-          acc[mt][n][3] = __fmaf_rn(shi.y, X1[n], __fmaf_rn(shi.x, d[3], acc[mt][n][3]));
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t a0 = nib_pair(wl[i][mt].x, j), a1 = nib_pair(wh[i][mt].x, j);
+              const uint32_t a2 = nib_pair(wl[i][mt].y, j), a3 = nib_pair(wh[i][mt].y, j);
+#pragma unroll
+              for (int n = 0; n < NT8; ++n)
+                if (n == 0 || n1_live) mma_bf16_16816(d[n], a0, a1, a2, a3, bf[n][2 * j], bf[n][2 * j + 1]);
+            }
+#pragma unroll
+            for (int n = 0; n < NT8; ++n) {
+              if (n == 0 || n1_live) {
+                acc[mt][n][0] = __fmaf_rn(slo.y, X0[n], __fmaf_rn(slo.x, d[n][0], acc[mt][n][0]));
+                acc[mt][n][1] = __fmaf_rn(slo.y, X1[n], __fmaf_rn(slo.x, d[n][1], acc[mt][n][1]));
+                acc[mt][n][2] = __fmaf_rn(shi.y, X0[n], __fmaf_rn(shi.x, d[n][2], acc[mt][n][2]));
+                acc[mt][n][3] = __fmaf_rn(shi.y, X1[n], __fmaf_rn(shi.x, d[n][3], acc[mt][n][3]));
+              }
+            }
+          }
+          load_group(i, g + kPF);
         }
-      }
-#pragma unroll
-      for (int mt = 0; mt < TL::kMTiles; ++mt) {
-        wlo[mt] = nlo[mt];
-        whi[mt] = nhi[mt];
       }
     }
 
     // ---- cross-warp reduction (warp order 0,1,2,3) through shared memory
-    __syncthreads();  // everyone is done reading xs, xsum and sc for this chunk
+    __syncthreads();  // everyone is done reading xs and xsum for this chunk
     float* red = reinterpret_cast<float*>(smem);
-    constexpr int kPer = TL::kMTiles * NT8 * 4;
+    constexpr int kPer = MT * NT8 * 4;
     if (warp > 0) {
 #pragma unroll
-      for (int mt = 0; mt < TL::kMTiles; ++mt)
+      for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
         for (int n = 0; n < NT8; ++n)
 #pragma unroll
@@ -266,7 +309,7 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a) {
 #pragma unroll
       for (int w = 0; w < kWarps - 1; ++w)
 #pragma unroll
-        for (int mt = 0; mt < TL::kMTiles; ++mt)
+        for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
           for (int n = 0; n < NT8; ++n)
 #pragma unroll
@@ -291,7 +334,7 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a) {
               }
             } else {
 #pragma unroll
-              for (int mt = 0; mt < TL::kMTiles; ++mt) {
+              for (int mt = 0; mt < MT; ++mt) {
                 const int row = n0 + mt * 16 + rsub;
                 if (row < N) o[row] = f2bf(acc[mt][n][i]);
               }
