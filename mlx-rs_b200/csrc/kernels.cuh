@@ -67,7 +67,6 @@ struct QgemvArgs {
   int N, K;
   uint16_t* out;            // [rows, N] bf16
   int out_mode;             // 0: row = pos, 1: row = perm[pos]
-  int sc_offset;            // set by the launcher: byte offset of the scale table in smem
 };
 
 struct CombineArgs {
