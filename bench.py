@@ -358,6 +358,7 @@ def main():
             bytes_ = na * wb["per_expert"] + wb["router"]
             sweep[f"T{Ts}"] = {"tokens_per_s": Ts / (statistics.median(tms) / 1e3),
                                "ms": statistics.median(tms), "experts": na,
+                               "stage_us": {kk: round(vv * 1e3, 2) for kk, vv in st.items()},
                                "block_GBps": bytes_ / (statistics.median(tms) / 1e3) / 1e9}
 
     cpu = cpu_baseline(bw_host, xs_host[0], args.cpu_seconds) if (rank == 0 and world == 1) else None

@@ -5,10 +5,10 @@
 // shared expert (:385-390) when each expert sees few tokens.
 //
 // One warp = one work unit = (expert, MT m16 tiles of weight rows) over the whole K and
-// all of the expert's tokens (in chunks of 8*NT8). Warps are independent: no shared
-// memory, no block barriers. Weights stream from HBM into registers (ld.global.nc,
+// all of the expert's tokens (in chunks of 8*NT8). Weights stream from HBM into registers (ld.global.nc,
 // 8 bytes = 16 nibbles per lane per row per group of 64) through a ring of kPF groups
-// kept in flight; activations are read from L1/L2. The int4 fields become bf16 pairs
+// kept in flight. The expert's token rows are staged once per CTA in shared memory
+// (cp.async); the 4 warps of a CTA work on the same expert. The int4 fields become bf16 pairs
 // holding 128 + q with one LOP3 per pair (exact) and feed mma.sync.m16n8k16 with the
 // weight rows as the M side and tokens as the N side. Each group of 64 is accumulated
 // separately and folded in fp32:
@@ -70,19 +70,27 @@ struct RowMap {
   }
 };
 
-MOE_DEV uint4 ldg_u4(const uint16_t* p) { return *reinterpret_cast<const uint4*>(p); }
+MOE_DEV uint4 lds_u4(const uint16_t* p) {
+  uint4 v;
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
 
 }  // namespace
 
+// Shared memory: the CTA's token rows, [8*NT8][K] bf16 in natural order with a
+// 16-byte pad per row (the pad makes the per-lane 16-byte reads conflict-free).
 template <bool GATED, int MT, int NT8>
-__global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a, int units_per_expert, int max_slots) {
+__global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a, int units_per_expert, int ctas_per_expert,
+                                                    int max_slots) {
   constexpr int kPF = 8;
   constexpr int ROWS = GATED ? 8 * MT : 16 * MT;  // output rows per unit
-  const int lane = threadIdx.x & 31;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gq = lane >> 2, cq = lane & 3;
-  const int wg = blockIdx.x * 4 + (threadIdx.x >> 5);
-  const int slot = wg / units_per_expert;
-  const int ut = wg - slot * units_per_expert;
+  const int slot = blockIdx.x / ctas_per_expert;
+  const int ut = (blockIdx.x - slot * ctas_per_expert) * 4 + warp;
   if (slot >= max_slots) return;
   if (a.n_active && slot >= *a.n_active) return;
   const int e = a.active ? a.active[slot] : slot;
@@ -91,8 +99,10 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a, int units_per_e
   if (row_end <= row_begin) return;
   const int K = a.K, N = a.N, G = K >> 6, wpr = K >> 3;
   const int r0 = ut * ROWS;
-  if (r0 >= N) return;
+  const bool unit_live = ut < units_per_expert && r0 < N;  // warp-uniform; the warp still stages
   const RowMap rm{a.x_mode, a.x_repeat, a.lhs, a.perm};
+  const int xs_stride = K + 8;  // elements
+  uint16_t* xs = reinterpret_cast<uint16_t*>(smem);
 
   // lane's two A rows per tile: lo = MMA row gq, hi = MMA row gq + 8
   const uint32_t* wlo[MT];
@@ -140,17 +150,32 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a, int units_per_e
   for (int64_t cbase = row_begin; cbase < row_end; cbase += 8 * NT8) {
     const int ntok = (row_end - cbase < 8 * NT8) ? (int)(row_end - cbase) : 8 * NT8;
     const bool n1_live = NT8 > 1 && ntok > 8;
+    if (unit_live) {
+#pragma unroll
+      for (int i = 0; i < kPF; ++i) load_group(i, i);
+    }
+    // ---- stage the chunk's token rows (cp.async, 16 bytes per copy)
+    __syncthreads();  // the previous chunk's readers are done
+    {
+      const int cpr = K >> 3;  // 16-byte pieces per row
+      for (int idx = tid; idx < ntok * cpr; idx += 128) {
+        const int t = idx / cpr, c = idx - t * cpr;
+        const uint16_t* src = a.x + (size_t)rm.xrow(cbase + t) * K + c * 8;
+        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(xs + (size_t)t * xs_stride + c * 8);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src));
+      }
+      asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+    }
+    __syncthreads();
     const uint16_t* xp[NT8];
     bool xv[NT8];
 #pragma unroll
     for (int n = 0; n < NT8; ++n) {
       const int t = n * 8 + gq;
       xv[n] = t < ntok;
-      xp[n] = a.x + (size_t)(xv[n] ? rm.xrow(cbase + t) : 0) * K + 16 * cq;
+      xp[n] = xs + (size_t)(xv[n] ? t : 0) * xs_stride + 16 * cq;
     }
-#pragma unroll
-    for (int i = 0; i < kPF; ++i) load_group(i, i);
-
+    if (!unit_live) continue;
     float acc[MT][NT8][4];
 #pragma unroll
     for (int t = 0; t < MT; ++t)
@@ -171,7 +196,7 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a, int units_per_e
           for (int n = 0; n < NT8; ++n) {
             uint32_t in[8];
             if (xv[n] && (n == 0 || n1_live)) {
-              const uint4 v0 = ldg_u4(xp[n] + g * 64), v1 = ldg_u4(xp[n] + g * 64 + 8);
+              const uint4 v0 = lds_u4(xp[n] + g * 64), v1 = lds_u4(xp[n] + g * 64 + 8);
               in[0] = v0.x; in[1] = v0.y; in[2] = v0.z; in[3] = v0.w;
               in[4] = v1.x; in[5] = v1.y; in[6] = v1.z; in[7] = v1.w;
             } else {
@@ -256,10 +281,21 @@ template <bool GATED, int MT, int NT8>
 static cudaError_t launch_qgemv_t(const QgemvArgs& a, int slots, cudaStream_t st) {
   constexpr int ROWS = GATED ? 8 * MT : 16 * MT;
   const int upe = (a.N + ROWS - 1) / ROWS;
-  const long long warps = (long long)upe * slots;
-  const long long blocks = (warps + 3) / 4;
+  const int cpe = (upe + 3) / 4;
+  const long long blocks = (long long)cpe * slots;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  qgemv_kernel<GATED, MT, NT8><<<(unsigned)blocks, 128, 0, st>>>(a, upe, slots);
+  const size_t smem = (size_t)8 * NT8 * (a.K + 8) * sizeof(uint16_t);
+  if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
+  auto kern = qgemv_kernel<GATED, MT, NT8>;
+  static thread_local int set_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != set_dev) {
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (err != cudaSuccess) return err;
+    set_dev = dev;
+  }
+  kern<<<(unsigned)blocks, 128, smem, st>>>(a, upe, cpe, slots);
   return cudaGetLastError();
 }
 
