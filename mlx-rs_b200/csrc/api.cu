@@ -288,7 +288,8 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   const int E = cfg->num_experts, H = cfg->hidden, I = cfg->moe_inter, k = cfg->top_k;
   const int64_t P = T * k;
   const int slots = (int)std::min<int64_t>(P, E);
-  const int max_rows = (int)std::min<int64_t>(T, 16);
+  // Token chunk of the decode GEMV: 8 rows (an expert with more rows takes more chunks).
+  const int max_rows = 8;
 
   // SwitchGLU gate/up + SiLU*up over grouped rows (x row = pair / k).
   moe::QgemvArgs gu = qgemv_args(wts->gate, &wts->up, I, H);

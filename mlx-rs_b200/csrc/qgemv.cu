@@ -79,12 +79,25 @@ MOE_DEV uint4 lds_u4(const uint16_t* p) {
 
 }  // namespace
 
-// Shared memory: the CTA's token rows, [8*NT8][K] bf16 in natural order with a
-// 16-byte pad per row (the pad makes the per-lane 16-byte reads conflict-free).
+// Shared memory: [x tile: 8*NT8 token rows x (K + 8) bf16][per-warp weight rings].
+// A warp's ring holds kStages chunks of kKC groups for its MT*16 weight rows; a row's
+// kKC groups (kKC*32 bytes, contiguous in global memory) are copied with 16-byte
+// cp.async and stored at a row stride of kKC*32 + 32 bytes, which makes the lanes'
+// 8-byte fragment reads conflict-free.
+template <int MT>
+struct Ring {
+  static constexpr int kKC = 4;                    // groups per chunk
+  static constexpr int kStages = 3;                // chunks in flight + being read
+  static constexpr int kRowBytes = kKC * 32 + 32;  // padded row stride
+  static constexpr int kRows = MT * 16;
+  static constexpr int kStageBytes = kRows * kRowBytes;
+  static constexpr int kWarpBytes = kStages * kStageBytes;
+};
+
 template <bool GATED, int MT, int NT8>
 __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a, int units_per_expert, int ctas_per_expert,
                                                     int max_slots) {
-  constexpr int kPF = 8;
+  using R = Ring<MT>;
   constexpr int ROWS = GATED ? 8 * MT : 16 * MT;  // output rows per unit
   extern __shared__ __align__(16) unsigned char smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -103,10 +116,48 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a, int units_per_e
   const RowMap rm{a.x_mode, a.x_repeat, a.lhs, a.perm};
   const int xs_stride = K + 8;  // elements
   uint16_t* xs = reinterpret_cast<uint16_t*>(smem);
+  unsigned char* ring = smem + (size_t)8 * NT8 * xs_stride * 2 + (size_t)warp * R::kWarpBytes;
+  const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring);
 
-  // lane's two A rows per tile: lo = MMA row gq, hi = MMA row gq + 8
-  const uint32_t* wlo[MT];
-  const uint32_t* whi[MT];
+  // ring row -> global row (gated: ring rows 0-7 of a tile are gate rows, 8-15 up rows)
+  auto grow = [&](int rr, const uint32_t*& W, bool& ok) -> size_t {
+    const int t = rr >> 4, r = rr & 15;
+    int row;
+    if (GATED) {
+      row = r0 + 8 * t + (r & 7);
+      W = (r < 8) ? a.w0 : a.w1;
+    } else {
+      row = r0 + 16 * t + r;
+      W = a.w0;
+    }
+    ok = row < N;
+    return (size_t)e * N + (ok ? row : 0);
+  };
+  // issue the cp.async copies of chunk c into ring stage c % kStages
+  auto issue_chunk = [&](int c) {
+    const int g0 = c * R::kKC;
+    const int ng = min(R::kKC, G - g0);
+    const uint32_t st = ring_s + (uint32_t)((c % R::kStages) * R::kStageBytes);
+#pragma unroll
+    for (int i = 0; i < MT * R::kKC; ++i) {
+      const int q = i * 32 + lane;           // 16-byte piece of the stage
+      const int rr = q / (2 * R::kKC);       // ring row
+      const int part = q - rr * 2 * R::kKC;  // piece within the row's kKC groups
+      if ((part >> 1) < ng) {
+        const uint32_t* W;
+        bool ok;
+        const size_t row = grow(rr, W, ok);
+        if (ok) {
+          const uint32_t* src = W + row * wpr + (size_t)g0 * 8 + part * 4;
+          const uint32_t dst = st + rr * R::kRowBytes + part * 16;
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src));
+        }
+      }
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  };
+
+  // lane's scale rows per tile: lo = MMA row gq, hi = MMA row gq + 8
   const uint16_t* slo[MT];
   const uint16_t* blo[MT];
   const uint16_t* shi[MT];
@@ -114,45 +165,30 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a, int units_per_e
   bool oklo[MT], okhi[MT];
 #pragma unroll
   for (int t = 0; t < MT; ++t) {
-    int rl, rh;
-    const uint32_t *Wl, *Wh;
-    const uint16_t *Sl, *Bl, *Sh, *Bh;
-    if (GATED) {
-      rl = rh = r0 + 8 * t + gq;
-      Wl = a.w0; Sl = a.s0; Bl = a.b0;
-      Wh = a.w1; Sh = a.s1; Bh = a.b1;
-    } else {
-      rl = r0 + 16 * t + gq;
-      rh = rl + 8;
-      Wl = Wh = a.w0; Sl = Sh = a.s0; Bl = Bh = a.b0;
-    }
-    oklo[t] = rl < N;
-    okhi[t] = rh < N;
-    const size_t ol = (size_t)e * N + (oklo[t] ? rl : 0), oh = (size_t)e * N + (okhi[t] ? rh : 0);
-    wlo[t] = Wl + ol * wpr + 2 * cq;
-    whi[t] = Wh + oh * wpr + 2 * cq;
+    const uint32_t* W;
+    const size_t ol = grow(t * 16 + gq, W, oklo[t]);
+    const size_t oh = grow(t * 16 + gq + 8, W, okhi[t]);
+    const uint16_t* Sl = a.s0;
+    const uint16_t* Bl = a.b0;
+    const uint16_t* Sh = GATED ? a.s1 : a.s0;
+    const uint16_t* Bh = GATED ? a.b1 : a.b0;
     slo[t] = Sl + ol * G;
     shi[t] = Sh + oh * G;
     blo[t] = Bl ? Bl + ol * G : nullptr;
     bhi[t] = Bh ? Bh + oh * G : nullptr;
   }
-
-  uint2 wl[kPF][MT], wh[kPF][MT];
-  auto load_group = [&](int ring, int g) {
-#pragma unroll
-    for (int t = 0; t < MT; ++t) {
-      const bool go = g < G;
-      wl[ring][t] = (go && oklo[t]) ? ldg_nc_u2(wlo[t] + g * 8) : make_uint2(0, 0);
-      wh[ring][t] = (go && okhi[t]) ? ldg_nc_u2(whi[t] + g * 8) : make_uint2(0, 0);
-    }
-  };
+  const int nchunks = (G + R::kKC - 1) / R::kKC;
 
   for (int64_t cbase = row_begin; cbase < row_end; cbase += 8 * NT8) {
     const int ntok = (row_end - cbase < 8 * NT8) ? (int)(row_end - cbase) : 8 * NT8;
     const bool n1_live = NT8 > 1 && ntok > 8;
+    // ---- weight ring prologue (its latency overlaps the activation staging)
     if (unit_live) {
 #pragma unroll
-      for (int i = 0; i < kPF; ++i) load_group(i, i);
+      for (int c = 0; c < R::kStages - 1; ++c) {
+        if (c < nchunks) issue_chunk(c);
+        else asm volatile("cp.async.commit_group;\n" ::: "memory");
+      }
     }
     // ---- stage the chunk's token rows (cp.async, 16 bytes per copy)
     __syncthreads();  // the previous chunk's readers are done
@@ -164,9 +200,11 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a, int units_per_e
         const uint32_t dst = (uint32_t)__cvta_generic_to_shared(xs + (size_t)t * xs_stride + c * 8);
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src));
       }
-      asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+      asm volatile("cp.async.commit_group;\n" ::: "memory");
+      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     }
     __syncthreads();
+    if (!unit_live) continue;
     const uint16_t* xp[NT8];
     bool xv[NT8];
 #pragma unroll
@@ -175,7 +213,7 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a, int units_per_e
       xv[n] = t < ntok;
       xp[n] = xs + (size_t)(xv[n] ? t : 0) * xs_stride + 16 * cq;
     }
-    if (!unit_live) continue;
+    // The staging wait above drained the ring prologue too; re-establish the ring.
     float acc[MT][NT8][4];
 #pragma unroll
     for (int t = 0; t < MT; ++t)
@@ -184,12 +222,15 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a, int units_per_e
 #pragma unroll
         for (int q = 0; q < 4; ++q) acc[t][n][q] = 0.0f;
 
-    for (int gb = 0; gb < G; gb += kPF) {
+    for (int c = 0; c < nchunks; ++c) {
+      // chunk c is complete when at most kStages-2 newer groups are pending
+      asm volatile("cp.async.wait_group %0;\n" ::"n"(R::kStages - 2) : "memory");
+      __syncwarp();
+      const unsigned char* st = ring + (c % R::kStages) * R::kStageBytes;
 #pragma unroll
-      for (int i = 0; i < kPF; ++i) {
-        const int g = gb + i;
+      for (int gl = 0; gl < R::kKC; ++gl) {
+        const int g = c * R::kKC + gl;
         if (g < G) {
-          // activations of this group: B fragments and per-token group sums
           uint32_t bf[NT8][8];
           float X0[NT8], X1[NT8];
 #pragma unroll
@@ -225,6 +266,8 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a, int units_per_e
             const float s_h = okhi[t] ? bf2f(shi[t][g]) : 0.0f;
             const float c_l = __fmaf_rn(-128.0f, s_l, (oklo[t] && blo[t]) ? bf2f(blo[t][g]) : 0.0f);
             const float c_h = __fmaf_rn(-128.0f, s_h, (okhi[t] && bhi[t]) ? bf2f(bhi[t][g]) : 0.0f);
+            const uint2 wlo = *reinterpret_cast<const uint2*>(st + (t * 16 + gq) * R::kRowBytes + gl * 32 + cq * 8);
+            const uint2 whi = *reinterpret_cast<const uint2*>(st + (t * 16 + gq + 8) * R::kRowBytes + gl * 32 + cq * 8);
             float d[NT8][4];
 #pragma unroll
             for (int n = 0; n < NT8; ++n)
@@ -232,8 +275,8 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a, int units_per_e
               for (int q = 0; q < 4; ++q) d[n][q] = 0.0f;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const uint32_t a0 = nib_pair(wl[i][t].x, j), a1 = nib_pair(wh[i][t].x, j);
-              const uint32_t a2 = nib_pair(wl[i][t].y, j), a3 = nib_pair(wh[i][t].y, j);
+              const uint32_t a0 = nib_pair(wlo.x, j), a1 = nib_pair(whi.x, j);
+              const uint32_t a2 = nib_pair(wlo.y, j), a3 = nib_pair(whi.y, j);
 #pragma unroll
               for (int n = 0; n < NT8; ++n)
                 if (n == 0 || n1_live) mma_bf16_16816(d[n], a0, a1, a2, a3, bf[n][2 * j], bf[n][2 * j + 1]);
@@ -246,17 +289,20 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a, int units_per_e
               acc[t][n][3] = __fmaf_rn(c_h, X1[n], __fmaf_rn(s_h, d[n][3], acc[t][n][3]));
             }
           }
-          load_group(i, g + kPF);
         }
       }
+      __syncwarp();  // every lane is done with this stage before it is refilled
+      if (c + R::kStages - 1 < nchunks) issue_chunk(c + R::kStages - 1);
+      else asm volatile("cp.async.commit_group;\n" ::: "memory");
     }
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
 
     // ---- epilogue: C fragment (MMA rows gq / gq+8, tokens 2cq / 2cq+1)
 #pragma unroll
     for (int n = 0; n < NT8; ++n)
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int tok = n * 8 + 2 * cq + c;
+      for (int cc = 0; cc < 2; ++cc) {
+        const int tok = n * 8 + 2 * cq + cc;
         if (tok < ntok) {
           const int64_t pos = cbase + tok;
           const int64_t orow = a.out_mode == 0 ? pos : rm.orig(pos);
@@ -265,11 +311,11 @@ __global__ void __launch_bounds__(128) qgemv_kernel(QgemvArgs a, int units_per_e
           for (int t = 0; t < MT; ++t) {
             if (GATED) {
               const int row = r0 + 8 * t + gq;
-              if (row < N) o[row] = swiglu_bf16(rbf(acc[t][n][c]), rbf(acc[t][n][2 + c]));
+              if (row < N) o[row] = swiglu_bf16(rbf(acc[t][n][cc]), rbf(acc[t][n][2 + cc]));
             } else {
               const int row = r0 + 16 * t + gq;
-              if (row < N) o[row] = f2bf(acc[t][n][c]);
-              if (row + 8 < N) o[row + 8] = f2bf(acc[t][n][2 + c]);
+              if (row < N) o[row] = f2bf(acc[t][n][cc]);
+              if (row + 8 < N) o[row + 8] = f2bf(acc[t][n][2 + cc]);
             }
           }
         }
@@ -284,7 +330,7 @@ static cudaError_t launch_qgemv_t(const QgemvArgs& a, int slots, cudaStream_t st
   const int cpe = (upe + 3) / 4;
   const long long blocks = (long long)cpe * slots;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  const size_t smem = (size_t)8 * NT8 * (a.K + 8) * sizeof(uint16_t);
+  const size_t smem = (size_t)8 * NT8 * (a.K + 8) * sizeof(uint16_t) + 4 * (size_t)Ring<MT>::kWarpBytes;
   if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
   auto kern = qgemv_kernel<GATED, MT, NT8>;
   static thread_local int set_dev = -1;
