@@ -10,6 +10,8 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <new>
 #include <string>
 
@@ -566,6 +568,16 @@ int moe_block_profile(moe_ctx* ctx, const moe_block_config* cfg, const moe_block
 }
 
 }  // extern "C"
+
+namespace moe {
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("MOE_B200_PDL");
+    return !(v && std::strcmp(v, "0") == 0);
+  }();
+  return on;
+}
+}  // namespace moe
 
 // Accessors for moe_gather_qmm_noalloc (api_noalloc.cu), which must not reach the
 // context's scratch.

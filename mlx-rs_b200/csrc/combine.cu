@@ -18,6 +18,8 @@ namespace moe {
 __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
   const int vec_per_row = a.H >> 3;
   const int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();
+  pdl_trigger();
   if (id >= (int64_t)a.T * vec_per_row) return;
   const int t = (int)(id / vec_per_row);
   const int h = (int)(id - (int64_t)t * vec_per_row) * 8;
@@ -63,6 +65,8 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const uint16_t* __restric
                                                        int64_t rows, int dim, uint16_t* __restrict__ out) {
   const int lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  pdl_wait();
+  pdl_trigger();
   if (r >= rows) return;
   const uint16_t* xr = x + (size_t)r * dim;
   const int nchunks = dim >> 3;
@@ -99,15 +103,13 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const uint16_t* __restric
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st) {
   const int64_t n = (int64_t)a.T * (a.H >> 3);
   if (n <= 0) return cudaSuccess;
-  combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a);
-  return cudaGetLastError();
+  return launch_k(combine_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, a);
 }
 
 cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, float eps, int64_t rows, int dim,
                             uint16_t* out, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
-  rms_norm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(x, w, eps, rows, dim, out);
-  return cudaGetLastError();
+  return launch_k(rms_norm_kernel, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0, st, x, w, eps, rows, dim, out);
 }
 
 }  // namespace moe

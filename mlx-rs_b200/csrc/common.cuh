@@ -66,4 +66,12 @@ MOE_DEV uint16_t swiglu_bf16(float g, float u) {
   return f2bf(__fmul_rn(a, u));
 }
 
+// Programmatic dependent launch: kernels of the block are launched so that each may
+// start while its predecessor in the stream drains. pdl_wait() blocks until the
+// predecessor grid has completed and its writes are visible (a no-op when the kernel
+// was launched normally); it must precede every read of a predecessor's output.
+// pdl_trigger() lets the next kernel start launching once every CTA has called it.
+MOE_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+MOE_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
 }  // namespace moe

@@ -6,7 +6,11 @@
 // bit for bit: offsets[e] = exclusive prefix sum of the counts, and within expert e
 // the pairs p = t*k + j appear in ascending p.
 //
-// Three launches over segments of `seg` consecutive pairs:
+// Small inputs (P <= 32768, E <= 512) take one launch of one CTA (group_small_kernel):
+// 32 warps each own a contiguous segment of the pairs; per-warp histograms in shared
+// memory give every warp its per-expert base, and each warp then ranks its pairs in
+// order with __match_any_sync. Larger inputs take three launches over segments of
+// `seg` consecutive pairs:
 //   hist:    per-segment histograms (shared-memory atomics; counts are order-free);
 //   scan:    one CTA: per-expert prefix over segments, exclusive scan over experts,
 //            the ascending list of active experts;
@@ -17,9 +21,96 @@
 
 namespace moe {
 
+// Block-wide exclusive scan of one value per thread (thread order); returns the
+// exclusive prefix and writes the total to *total (1024 threads).
+MOE_DEV int32_t block_exclusive_scan(int32_t v, int32_t* warp_tot, int32_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int32_t incl = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int32_t u = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += u;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int32_t w = warp_tot[lane];
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int32_t u = __shfl_up_sync(0xffffffffu, w, off);
+      if (lane >= off) w += u;
+    }
+    warp_tot[lane] = w;
+  }
+  __syncthreads();
+  const int32_t excl = incl - v + (warp > 0 ? warp_tot[warp - 1] : 0);
+  if (total) *total = warp_tot[31];
+  __syncthreads();
+  return excl;
+}
+
+// One CTA of 1024 threads. Shared memory: wbase[32][E] per-warp counts, then bases.
+__global__ void __launch_bounds__(1024) group_small_kernel(GroupArgs a) {
+  extern __shared__ int32_t wbase[];
+  __shared__ int32_t warp_tot[32];
+  __shared__ int32_t n_act;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int E = a.E;
+  pdl_wait();
+  for (int i = tid; i < 32 * E; i += 1024) wbase[i] = 0;
+  __syncthreads();
+  const int64_t seg = (a.P + 31) / 32;
+  const int64_t p0 = warp * seg;
+  const int64_t p1 = (p0 + seg < a.P) ? p0 + seg : a.P;
+  for (int64_t p = p0 + lane; p < p1; p += 32) {
+    const uint32_t e = a.key[p];
+    if (e < (uint32_t)E) atomicAdd(&wbase[warp * E + e], 1);
+  }
+  __syncthreads();
+  // per expert (thread e): prefix over warps; expert totals
+  int32_t tot = 0;
+  if (tid < E) {
+    for (int w = 0; w < 32; ++w) {
+      const int32_t h = wbase[w * E + tid];
+      wbase[w * E + tid] = tot;
+      tot += h;
+    }
+  }
+  const int32_t base = block_exclusive_scan(tid < E ? tot : 0, warp_tot, nullptr);
+  const int32_t arank = block_exclusive_scan((tid < E && tot > 0) ? 1 : 0, warp_tot, &n_act);
+  if (tid < E) {
+    a.offsets[tid] = base;
+    if (tot > 0) a.active[arank] = tid;
+    for (int w = 0; w < 32; ++w) wbase[w * E + tid] += base;
+  }
+  if (tid == E) a.offsets[E] = base;  // thread E holds the exclusive total of experts 0..E-1
+  if (tid == 0) *a.n_active = n_act;
+  pdl_trigger();
+  __syncthreads();
+  // stable scatter: warp w walks its segment in order, 32 pairs at a time
+  int32_t* cur = wbase + warp * E;
+  for (int64_t b = p0; b < p1; b += 32) {
+    const int64_t p = b + lane;
+    const bool valid = p < p1;
+    const uint32_t e = valid ? a.key[p] : 0xffffffffu;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const unsigned lt = (1u << lane) - 1u;
+    int32_t pos = 0;
+    if (valid && e < (uint32_t)E) {
+      pos = cur[e] + __popc(peers & lt);
+      a.perm[pos] = (uint32_t)p;
+      if (a.inv) a.inv[p] = (uint32_t)pos;
+    }
+    __syncwarp();
+    if (valid && e < (uint32_t)E && (peers >> lane) == 1u) cur[e] = pos + 1;
+    __syncwarp();
+  }
+}
+
 __global__ void group_hist_kernel(GroupArgs a) {
   extern __shared__ int32_t sh[];
   const int g = blockIdx.x;
+  pdl_wait();
   for (int e = threadIdx.x; e < a.E; e += blockDim.x) sh[e] = 0;
   __syncthreads();
   const int64_t p0 = (int64_t)g * a.seg;
@@ -38,6 +129,7 @@ __global__ void __launch_bounds__(1024) group_scan_kernel(GroupArgs a) {
   __shared__ int32_t warp_act[32];
   constexpr int EPT = 4;
   const int tid = threadIdx.x;
+  pdl_wait();
   int32_t tot[EPT];
   int32_t my_sum = 0, my_act = 0;
 #pragma unroll
@@ -99,16 +191,15 @@ __global__ void __launch_bounds__(1024) group_scan_kernel(GroupArgs a) {
       base += tot[i];
     }
   }
-  if (tid == 0) {
-    a.offsets[a.E] = (int32_t)a.P;
-    *a.n_active = warp_act[31];
-  }
+  if (tid == 0) *a.n_active = warp_act[31];
+  if (tid * EPT < a.E && (tid + 1) * EPT >= a.E) a.offsets[a.E] = base;  // total of valid pairs
 }
 
 __global__ void group_scatter_kernel(GroupArgs a) {
   extern __shared__ int32_t cur[];
   const int g = blockIdx.x;
   const int lane = threadIdx.x;
+  pdl_wait();
   for (int e = lane; e < a.E; e += 32) cur[e] = a.segbase[(size_t)g * a.E + e];
   __syncwarp();
   const int64_t p0 = (int64_t)g * a.seg;
@@ -139,11 +230,25 @@ cudaError_t launch_group(const GroupArgs& a, cudaStream_t st) {
     if (err != cudaSuccess) return err;
     return cudaMemsetAsync(a.n_active, 0, sizeof(int32_t), st);
   }
+  if (a.P <= 32768 && a.E <= 512) {
+    const size_t smem = sizeof(int32_t) * 32 * a.E;
+    static thread_local int set_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev != set_dev) {
+      cudaError_t err = cudaFuncSetAttribute(group_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)(sizeof(int32_t) * 32 * 512));
+      if (err != cudaSuccess) return err;
+      set_dev = dev;
+    }
+    return launch_k(group_small_kernel, dim3(1), dim3(1024), smem, st, a);
+  }
   const size_t sh = sizeof(int32_t) * a.E;
-  group_hist_kernel<<<a.nseg, 256, sh, st>>>(a);
-  group_scan_kernel<<<1, 1024, 0, st>>>(a);
-  group_scatter_kernel<<<a.nseg, 32, sh, st>>>(a);
-  return cudaGetLastError();
+  cudaError_t err = launch_k(group_hist_kernel, dim3(a.nseg), dim3(256), sh, st, a);
+  if (err != cudaSuccess) return err;
+  err = launch_k(group_scan_kernel, dim3(1), dim3(1024), 0, st, a);
+  if (err != cudaSuccess) return err;
+  return launch_k(group_scatter_kernel, dim3(a.nseg), dim3(32), sh, st, a);
 }
 
 }  // namespace moe

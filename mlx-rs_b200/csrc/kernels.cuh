@@ -4,7 +4,29 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace moe {
+
+// Launches kern with programmatic stream serialisation (the kernel may begin while its
+// predecessor in the stream finishes; it calls pdl_wait() before reading the
+// predecessor's outputs). MOE_B200_PDL=0 in the environment launches normally.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                     Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // Router logits: logits[T, n_rows] = x[T, K] . dequant(W)^T in the canonical order.
 // Rows 0..E-1 come from the router weight; row E (when n_rows == E + 1) is the

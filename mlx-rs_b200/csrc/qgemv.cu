@@ -122,6 +122,7 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
   const int gq = lane >> 2, cq = lane & 3;
   const int slot = blockIdx.x / ctas_per_expert;
   const int ut = (blockIdx.x - slot * ctas_per_expert) * nwarps + warp;
+  pdl_wait();
   if (slot >= max_slots) return;
   if (a.n_active && slot >= *a.n_active) return;
   const int e = a.active ? a.active[slot] : slot;
@@ -329,6 +330,7 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
       __syncwarp();  // every lane is done with this stage before it is refilled
     }
     cp_wait<0>();
+    pdl_trigger();
 
     // ---- epilogue: C fragment (MMA rows gq / gq+8, tokens 2cq / 2cq+1)
 #pragma unroll
@@ -374,8 +376,7 @@ static cudaError_t launch_qgemv_t(const QgemvArgs& a, int slots, int wpc, cudaSt
     if (err != cudaSuccess) return err;
     set_dev = dev;
   }
-  kern<<<(unsigned)blocks, wpc * 32, smem, st>>>(a, upe, cpe, slots);
-  return cudaGetLastError();
+  return launch_k(kern, dim3((unsigned)blocks), dim3(wpc * 32), smem, st, a, upe, cpe, slots);
 }
 
 cudaError_t launch_qgemv(const QgemvArgs& a, bool gated, int slots, int max_rows_per_expert,

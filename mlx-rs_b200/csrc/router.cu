@@ -22,6 +22,7 @@ __global__ void __launch_bounds__(128) router_logits_kernel(RouterArgs a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int row0 = (blockIdx.x * 4 + warp) * NE;
   const int t0 = blockIdx.y * NT;
+  pdl_wait();
   if (row0 >= a.n_rows) return;
   const int nchunks = a.K >> 5;
   const int wpr = a.K >> 3;
@@ -103,6 +104,7 @@ __global__ void __launch_bounds__(128) router_logits_kernel(RouterArgs a) {
       for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
       acc[e][t] = v;
     }
+  pdl_trigger();
   if (lane == 0) {
 #pragma unroll
     for (int e = 0; e < NE; ++e)
@@ -127,6 +129,8 @@ template <int PL>
 __global__ void __launch_bounds__(128) topk_kernel(TopkArgs a) {
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
+  pdl_wait();
+  pdl_trigger();
   if (t >= a.T) return;
   const uint16_t* lrow = a.logits + (size_t)t * a.n_rows;
 
@@ -235,27 +239,24 @@ cudaError_t launch_router(const RouterArgs& a, cudaStream_t st) {
   if (a.T <= 0) return cudaSuccess;
   if (a.T <= 4) {
     dim3 grid((a.n_rows + 3) / 4, a.T);
-    router_logits_kernel<1, 1><<<grid, 128, 0, st>>>(a);
+    return launch_k(router_logits_kernel<1, 1>, grid, dim3(128), 0, st, a);
   } else if (a.T <= 64) {
     dim3 grid((a.n_rows + 7) / 8, (a.T + 3) / 4);
-    router_logits_kernel<2, 4><<<grid, 128, 0, st>>>(a);
-  } else {
-    dim3 grid((a.n_rows + 15) / 16, (a.T + 7) / 8);
-    router_logits_kernel<4, 8><<<grid, 128, 0, st>>>(a);
+    return launch_k(router_logits_kernel<2, 4>, grid, dim3(128), 0, st, a);
   }
-  return cudaGetLastError();
+  dim3 grid((a.n_rows + 15) / 16, (a.T + 7) / 8);
+  return launch_k(router_logits_kernel<4, 8>, grid, dim3(128), 0, st, a);
 }
 
 cudaError_t launch_topk(const TopkArgs& a, cudaStream_t st) {
   if (a.T <= 0) return cudaSuccess;
   const int blocks = (a.T + 3) / 4;
   const int pl = (a.E + 31) / 32;
-  if (pl <= 1) topk_kernel<1><<<blocks, 128, 0, st>>>(a);
-  else if (pl <= 2) topk_kernel<2><<<blocks, 128, 0, st>>>(a);
-  else if (pl <= 4) topk_kernel<4><<<blocks, 128, 0, st>>>(a);
-  else if (pl <= 8) topk_kernel<8><<<blocks, 128, 0, st>>>(a);
-  else topk_kernel<16><<<blocks, 128, 0, st>>>(a);
-  return cudaGetLastError();
+  if (pl <= 1) return launch_k(topk_kernel<1>, dim3(blocks), dim3(128), 0, st, a);
+  if (pl <= 2) return launch_k(topk_kernel<2>, dim3(blocks), dim3(128), 0, st, a);
+  if (pl <= 4) return launch_k(topk_kernel<4>, dim3(blocks), dim3(128), 0, st, a);
+  if (pl <= 8) return launch_k(topk_kernel<8>, dim3(blocks), dim3(128), 0, st, a);
+  return launch_k(topk_kernel<16>, dim3(blocks), dim3(128), 0, st, a);
 }
 
 }  // namespace moe
