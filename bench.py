@@ -35,7 +35,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "MoE-block tokens/s; decode HBM GB/s & prefill TFLOPS vs roofline at 1-8 GPU"
-LAUNCHES_PER_STEP = 8  # router, top-k, 3 grouping kernels, gate/up, down, combine
+LAUNCHES_PER_STEP = 6  # router, top-k, grouping (one CTA at this size), gate/up, down, combine
 
 
 def parse():

@@ -158,25 +158,39 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
     return W + ((size_t)e * N + row) * wpr;
   };
 
-  // per-lane cp.async sources (chunk 0) and swizzled destinations
+  // per-lane cp.async sources (advanced by one chunk per issue) and swizzled destinations
   const uint32_t* src[kPieces];
   uint32_t dst[kPieces];
+  int pgl[kPieces];
 #pragma unroll
   for (int i = 0; i < kPieces; ++i) {
     const int q = i * 32 + lane;
     const int rr = q >> 3, part = q & 7, gl = part >> 1, half = part & 1;
     src[i] = wrow(rr) + part * 4;
     dst[i] = rr * (kKC * 32) + ((gl ^ (rr & 3)) * 32) + half * 16;
+    pgl[i] = gl;
   }
   const int nchunks = (G + kKC - 1) / kKC;
+  const int tail_groups = G - (nchunks - 1) * kKC;  // groups in the last chunk
+  int issued = 0;  // chunks issued so far in this token chunk
+  auto reset_src = [&]() {
+#pragma unroll
+    for (int i = 0; i < kPieces; ++i) src[i] -= (size_t)issued * kKC * 8;
+    issued = 0;
+  };
   auto issue_chunk = [&](int c) {
     const uint32_t st = ring_s + (uint32_t)((c % kStages) * kStageBytes);
-    const int ng = G - c * kKC;
+    if (c + 1 < nchunks || tail_groups == kKC) {
 #pragma unroll
-    for (int i = 0; i < kPieces; ++i) {
-      const int gl = ((i * 32 + lane) & 7) >> 1;
-      if (gl < ng) cp_async16(st + dst[i], src[i] + c * kKC * 8);
+      for (int i = 0; i < kPieces; ++i) cp_async16(st + dst[i], src[i]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < kPieces; ++i)
+        if (pgl[i] < tail_groups) cp_async16(st + dst[i], src[i]);
     }
+#pragma unroll
+    for (int i = 0; i < kPieces; ++i) src[i] += kKC * 8;
+    ++issued;
     cp_commit();
   };
 
@@ -209,6 +223,7 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
 
   for (int64_t cbase = row_begin; cbase < row_end; cbase += kTok) {
     const int ntok = (row_end - cbase < kTok) ? (int)(row_end - cbase) : kTok;
+    reset_src();
     if (unit_live) issue_chunk(0);
     __syncthreads();  // the previous chunk's readers of xperm/xsum are done
     // ---- stage the token rows: fragment-order permutation + per-group sums
@@ -263,11 +278,9 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
 #pragma unroll
       for (int q = 0; q < 4; ++q) acc[t][q] = 0.0f;
 
-    for (int c = 0; c < nchunks; ++c) {
-      if (c + 1 < nchunks) issue_chunk(c + 1);
-      else cp_commit();
-      // per-chunk scales of the lane's rows: (s, b) for kKC groups
-      uint32_t sw[MT][2][2], bw[MT][2][2];  // [tile][lo/hi][pair of groups]
+    // scales of the lane's rows, (s, b) for kKC groups, loaded one chunk ahead
+    uint32_t sw[MT][2][2], bw[MT][2][2];  // [tile][lo/hi][pair of groups]
+    auto load_scales = [&](int c, uint32_t (&sv2)[MT][2][2], uint32_t (&bv2)[MT][2][2]) {
       const int g0 = c * kKC;
 #pragma unroll
       for (int t = 0; t < MT; ++t)
@@ -276,8 +289,8 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
           if (vec_scales) {
             const uint2 s2 = *reinterpret_cast<const uint2*>(sp[t][h] + g0);
             const uint2 b2 = bp[t][h] ? *reinterpret_cast<const uint2*>(bp[t][h] + g0) : make_uint2(0, 0);
-            sw[t][h][0] = s2.x; sw[t][h][1] = s2.y;
-            bw[t][h][0] = b2.x; bw[t][h][1] = b2.y;
+            sv2[t][h][0] = s2.x; sv2[t][h][1] = s2.y;
+            bv2[t][h][0] = b2.x; bv2[t][h][1] = b2.y;
           } else {
             uint16_t sv[kKC], bv[kKC];
 #pragma unroll
@@ -286,10 +299,18 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
               sv[i] = in ? sp[t][h][g0 + i] : 0;
               bv[i] = (in && bp[t][h]) ? bp[t][h][g0 + i] : 0;
             }
-            sw[t][h][0] = sv[0] | ((uint32_t)sv[1] << 16); sw[t][h][1] = sv[2] | ((uint32_t)sv[3] << 16);
-            bw[t][h][0] = bv[0] | ((uint32_t)bv[1] << 16); bw[t][h][1] = bv[2] | ((uint32_t)bv[3] << 16);
+            sv2[t][h][0] = sv[0] | ((uint32_t)sv[1] << 16); sv2[t][h][1] = sv[2] | ((uint32_t)sv[3] << 16);
+            bv2[t][h][0] = bv[0] | ((uint32_t)bv[1] << 16); bv2[t][h][1] = bv[2] | ((uint32_t)bv[3] << 16);
           }
         }
+    };
+    load_scales(0, sw, bw);
+    for (int c = 0; c < nchunks; ++c) {
+      if (c + 1 < nchunks) issue_chunk(c + 1);
+      else cp_commit();
+      uint32_t swn[MT][2][2], bwn[MT][2][2];
+      if (c + 1 < nchunks) load_scales(c + 1, swn, bwn);
+      const int g0 = c * kKC;
       cp_wait<1>();
       __syncwarp();
       const uint32_t st = ring_s + (uint32_t)((c % kStages) * kStageBytes);
@@ -328,6 +349,17 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
         }
       }
       __syncwarp();  // every lane is done with this stage before it is refilled
+      if (c + 1 < nchunks) {
+#pragma unroll
+        for (int t = 0; t < MT; ++t)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              sw[t][h][q] = swn[t][h][q];
+              bw[t][h][q] = bwn[t][h][q];
+            }
+      }
     }
     cp_wait<0>();
     pdl_trigger();
