@@ -91,6 +91,9 @@ int ensure_scratch(moe_ctx* ctx, size_t bytes) {
     return fail(ctx, MOE_ERR_NO_MEMORY, "scratch cudaMalloc(%zu) failed: %s", want, cudaGetErrorString(e));
   }
   ctx->scratch_bytes = want;
+  // the first word holds the device status (bounded waits that expired); start clean
+  e = cudaMemset(ctx->scratch, 0, 256);
+  if (e != cudaSuccess) return fail(ctx, MOE_ERR_CUDA, "scratch status reset failed: %s", cudaGetErrorString(e));
   return MOE_OK;
 }
 
@@ -124,6 +127,8 @@ struct BlockWs {
   uint16_t* ybuf;
   uint16_t* hs;
   uint16_t* ys;
+  int32_t* tile_start;
+  int32_t* status;
   size_t bytes;
 };
 
@@ -132,6 +137,7 @@ BlockWs carve_block(void* base, const moe_block_config* c, int64_t T) {
   BlockWs w{};
   const int64_t E = c->num_experts, P = T * c->top_k;
   const int64_t nseg = std::max<int64_t>(1, (P + kGroupSeg - 1) / kGroupSeg);
+  w.status = cv.take<int32_t>(64);  // first, at a fixed offset; zeroed when allocated
   w.logits = cv.take<uint16_t>(T * (E + 1));
   w.idx = cv.take<uint32_t>(P);
   w.wsel = cv.take<uint16_t>(P);
@@ -143,6 +149,7 @@ BlockWs carve_block(void* base, const moe_block_config* c, int64_t T) {
   w.n_active = cv.take<int32_t>(1);
   w.perm = cv.take<uint32_t>(P);
   w.inv = cv.take<uint32_t>(P);
+  w.tile_start = cv.take<int32_t>(E + 1);
   w.hbuf = cv.take<uint16_t>(P * c->moe_inter);
   w.ybuf = cv.take<uint16_t>(P * c->hidden);
   if (c->shared_inter > 0) {
@@ -244,9 +251,21 @@ int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* 
   ga.n_active = ws.n_active;
   ga.perm = ws.perm;
   ga.inv = ws.inv;
+  ga.tile_start = ws.tile_start;
+  ga.tile_rows = moe::kTcTileRows;
   MOE_MARK(ev, kGroup, ctx->stream);
   MOE_CUDA(ctx, moe::launch_group(ga, ctx->stream));
   return MOE_OK;
+}
+
+// Tensor-core (tcgen05) GEMM for many rows per expert, GEMV (mma.sync) for few.
+// MOE_B200_TC=0 / =1 in the environment forces one path (where the shape allows tc).
+bool use_tc(int64_t rows, int64_t experts, int N, int K) {
+  if (N % 128 != 0 || K % 64 != 0) return false;
+  const char* v = std::getenv("MOE_B200_TC");
+  if (v && v[0] == '0') return false;
+  if (v && v[0] == '1') return true;
+  return rows >= 32 * experts;
 }
 
 moe::QgemvArgs qgemv_args(const moe_qweight& m0, const moe_qweight* m1, int N, int K) {
@@ -293,6 +312,8 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   // Token chunk of the decode GEMV: 8 rows (an expert with more rows takes more chunks).
   const int max_rows = 8;
 
+  const bool tc_gu = use_tc(P, E, I, H), tc_dn = use_tc(P, E, H, I);
+  const int max_tiles = (int)(P / moe::kTcTileRows + std::min<int64_t>(E, P) + 1);
   // SwitchGLU gate/up + SiLU*up over grouped rows (x row = pair / k).
   moe::QgemvArgs gu = qgemv_args(wts->gate, &wts->up, I, H);
   gu.x = static_cast<const uint16_t*>(x);
@@ -305,7 +326,12 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   gu.out = ws.hbuf;
   gu.out_mode = 0;
   MOE_MARK(ev, kGateUp, ctx->stream);
-  MOE_CUDA(ctx, moe::launch_qgemv(gu, true, slots, max_rows, ctx->stream));
+  if (tc_gu) {
+    moe::TcGemmArgs ta{gu, ws.tile_start, E, max_tiles, ws.status};
+    MOE_CUDA(ctx, moe::launch_tc_gemm(ta, true, ctx->stream));
+  } else {
+    MOE_CUDA(ctx, moe::launch_qgemv(gu, true, slots, max_rows, ctx->stream));
+  }
 
   // down projection over the same grouped rows.
   moe::QgemvArgs dn = qgemv_args(wts->down, nullptr, H, I);
@@ -318,7 +344,12 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   dn.out = ws.ybuf;
   dn.out_mode = 0;
   MOE_MARK(ev, kDown, ctx->stream);
-  MOE_CUDA(ctx, moe::launch_qgemv(dn, false, slots, max_rows, ctx->stream));
+  if (tc_dn) {
+    moe::TcGemmArgs ta{dn, ws.tile_start, E, max_tiles, ws.status};
+    MOE_CUDA(ctx, moe::launch_tc_gemm(ta, false, ctx->stream));
+  } else {
+    MOE_CUDA(ctx, moe::launch_qgemv(dn, false, slots, max_rows, ctx->stream));
+  }
 
   const bool shared = cfg->shared_inter > 0;
   if (!shared) {
@@ -333,14 +364,25 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
     sgu.n_identity = (int)T;
     sgu.out = ws.hs;
     MOE_MARK(ev, kSharedGateUp, ctx->stream);
-    MOE_CUDA(ctx, moe::launch_qgemv(sgu, true, 1, max_rows, ctx->stream));
+    const int stiles = (int)((T + moe::kTcTileRows - 1) / moe::kTcTileRows);
+    if (use_tc(T, 1, Is, H)) {
+      moe::TcGemmArgs ta{sgu, nullptr, 1, stiles, ws.status};
+      MOE_CUDA(ctx, moe::launch_tc_gemm(ta, true, ctx->stream));
+    } else {
+      MOE_CUDA(ctx, moe::launch_qgemv(sgu, true, 1, max_rows, ctx->stream));
+    }
     moe::QgemvArgs sdn = qgemv_args(wts->shared_down, nullptr, H, Is);
     sdn.x = ws.hs;
     sdn.x_mode = 0;
     sdn.n_identity = (int)T;
     sdn.out = ws.ys;
     MOE_MARK(ev, kSharedDown, ctx->stream);
-    MOE_CUDA(ctx, moe::launch_qgemv(sdn, false, 1, max_rows, ctx->stream));
+    if (use_tc(T, 1, H, Is)) {
+      moe::TcGemmArgs ta{sdn, nullptr, 1, stiles, ws.status};
+      MOE_CUDA(ctx, moe::launch_tc_gemm(ta, false, ctx->stream));
+    } else {
+      MOE_CUDA(ctx, moe::launch_qgemv(sdn, false, 1, max_rows, ctx->stream));
+    }
   }
 
   moe::CombineArgs ca{};
@@ -554,10 +596,13 @@ int moe_block_profile(moe_ctx* ctx, const moe_block_config* cfg, const moe_block
     cudaError_t e = cudaEventSynchronize(ev[kStages]);
     for (int i = 0; i < kStages && e == cudaSuccess; ++i) e = cudaEventElapsedTime(&stage_ms[i], ev[i], ev[i + 1]);
     if (e != cudaSuccess) rc = fail(ctx, MOE_ERR_CUDA, "moe_block_profile: %s", cudaGetErrorString(e));
-    if (rc == MOE_OK && n_active) {
+    if (rc == MOE_OK) {
       BlockWs ws = carve_block(ctx->scratch, cfg, T);
-      e = cudaMemcpy(n_active, ws.n_active, sizeof(int32_t), cudaMemcpyDeviceToHost);
+      int32_t st = 0;
+      e = cudaMemcpy(&st, ws.status, sizeof(int32_t), cudaMemcpyDeviceToHost);
+      if (e == cudaSuccess && n_active) e = cudaMemcpy(n_active, ws.n_active, sizeof(int32_t), cudaMemcpyDeviceToHost);
       if (e != cudaSuccess) rc = fail(ctx, MOE_ERR_CUDA, "moe_block_profile: %s", cudaGetErrorString(e));
+      else if (st != 0) rc = fail(ctx, MOE_ERR_TIMEOUT, "moe_block_profile: a bounded device wait expired (status %d)", st);
     }
   } else if (rc == MOE_OK) {
     for (int i = 0; i < kStages; ++i) stage_ms[i] = 0.0f;

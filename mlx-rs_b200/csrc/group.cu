@@ -78,6 +78,11 @@ __global__ void __launch_bounds__(1024) group_small_kernel(GroupArgs a) {
   }
   const int32_t base = block_exclusive_scan(tid < E ? tot : 0, warp_tot, nullptr);
   const int32_t arank = block_exclusive_scan((tid < E && tot > 0) ? 1 : 0, warp_tot, &n_act);
+  if (a.tile_start) {
+    const int32_t nt = tid < E ? (tot + a.tile_rows - 1) / a.tile_rows : 0;
+    const int32_t tbase = block_exclusive_scan(nt, warp_tot, nullptr);
+    if (tid <= E) a.tile_start[tid] = tbase;
+  }
   if (tid < E) {
     a.offsets[tid] = base;
     if (tot > 0) a.active[arank] = tid;
@@ -193,6 +198,17 @@ __global__ void __launch_bounds__(1024) group_scan_kernel(GroupArgs a) {
   }
   if (tid == 0) *a.n_active = warp_act[31];
   if (tid * EPT < a.E && (tid + 1) * EPT >= a.E) a.offsets[a.E] = base;  // total of valid pairs
+  if (a.tile_start) {
+    __syncthreads();
+    if (tid == 0) {
+      int32_t run = 0;
+      for (int e = 0; e < a.E; ++e) {
+        a.tile_start[e] = run;
+        run += (a.offsets[e + 1] - a.offsets[e] + a.tile_rows - 1) / a.tile_rows;
+      }
+      a.tile_start[a.E] = run;
+    }
+  }
 }
 
 __global__ void group_scatter_kernel(GroupArgs a) {

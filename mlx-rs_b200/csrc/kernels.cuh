@@ -66,6 +66,8 @@ struct GroupArgs {
   int32_t* n_active;
   uint32_t* perm;   // [P] pos -> p
   uint32_t* inv;    // [P] p -> pos, may be null
+  int32_t* tile_start;  // [E + 1] exclusive prefix of ceil(count_e / tile_rows), may be null
+  int tile_rows;
 };
 
 // Grouped quantized GEMV/GEMM over expert-grouped rows (tensor cores via mma.sync,
@@ -108,6 +110,19 @@ cudaError_t launch_group(const GroupArgs& a, cudaStream_t st);
 // the token chunk the kernel stages at once; slots = grid.y.
 cudaError_t launch_qgemv(const QgemvArgs& a, bool gated, int slots, int max_rows_per_expert,
                          cudaStream_t st);
+// Grouped GEMM on tcgen05 tensor cores for the prefill regime (many rows per expert):
+// one CTA = 128 weight rows x up to 256 rows (tokens) of one expert. Requires N % 128 == 0
+// and K % 64 == 0. tile_start (from the grouping) maps CTAs to (expert, token tile).
+struct TcGemmArgs {
+  QgemvArgs q;                // operands, row mapping and output as for the GEMV
+  const int32_t* tile_start;  // [E + 1] prefix of 256-row tiles per expert (null: identity)
+  int num_experts;            // E (entries of tile_start minus one)
+  int max_tiles;              // grid.y
+  int32_t* status;            // device word: nonzero after a bounded wait expired
+};
+constexpr int kTcTileRows = 256;
+cudaError_t launch_tc_gemm(const TcGemmArgs& a, bool gated, cudaStream_t st);
+
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st);
 cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, float eps, int64_t rows, int dim,
                             uint16_t* out, cudaStream_t st);

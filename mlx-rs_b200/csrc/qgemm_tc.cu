@@ -1,0 +1,458 @@
+// qgemm_tc.cu — grouped 4-bit GEMM on tcgen05 tensor cores (prefill regime).
+//
+// Replaces gather_qmm / quantized_matmul (crates/mlx-core/src/ops.rs:592-637, 830-891)
+// for the SwitchGLU gate/up/down projections (qwen3_moe_python_port.rs:311-359) and the
+// shared expert (:385-390) when experts see many tokens.
+//
+// One CTA computes D[128 weight rows x n tokens] = W_tile . X_tile^T over the whole K
+// for one expert and one tile of up to 256 of its (grouped) token rows:
+//   * warps 0-3 (128 threads) are producers: per K step of 64 (one quantization group)
+//     they load the packed int4 rows, dequantise them to bf16 (w = RN_bf16(s*q + b), the
+//     value MLX's GPU qmm computes into threadgroup memory) and store them as the A tile,
+//     and copy the token rows with cp.async as the B tile; both tiles are K-major with
+//     the 128-byte swizzle the tensor core reads;
+//   * warp 4 allocates tensor memory and, from one lane, issues tcgen05.mma
+//     (kind::f16, bf16 x bf16 -> fp32, M=128, N=n rounded up to 16, K=16 per instruction)
+//     accumulating in TMEM; tcgen05.commit on an mbarrier frees each stage;
+//   * after the last stage the producer warps read the accumulators back with
+//     tcgen05.ld (warp w owns TMEM lanes 32w..32w+31 = weight rows) and write bf16
+//     outputs; in the gated form the gate and up accumulators (TMEM columns 0 and 256)
+//     are combined by SwiGLU in registers.
+// The shared-memory ring has kStages stages guarded by full/empty mbarriers. Every
+// mbarrier wait is bounded; on expiry the CTA records a status code and drains out.
+// No TMA and no cluster multicast are used.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace moe {
+
+namespace {
+
+constexpr int kBM = 128;                   // weight rows per CTA (MMA M)
+constexpr int kBN = kTcTileRows;           // max tokens per CTA (MMA N)
+constexpr int kBK = 64;                    // K per stage
+constexpr int kATileBytes = kBM * kBK * 2;   // 16 KB
+constexpr int kBTileBytes = kBN * kBK * 2;   // 32 KB
+constexpr int kProducers = 128;
+constexpr int kThreads = kProducers + 32;
+constexpr uint64_t kWaitLimitNs = 200ull * 1000 * 1000;  // bound of one mbarrier wait (200 ms)
+
+template <bool GATED>
+struct TcCfg {
+  static constexpr int kMats = GATED ? 2 : 1;
+  static constexpr int kStages = GATED ? 3 : 4;
+  static constexpr int kStageBytes = kMats * kATileBytes + kBTileBytes;
+  static constexpr int kTmemCols = GATED ? 512 : 256;
+  // [stages][A tiles..., B tile] | full[S] empty[S] done | tmem base | xrow[kBN]
+  static constexpr int kBarOffset = kStages * kStageBytes;
+  static constexpr int kSmemBytes = kBarOffset + 8 * (2 * kStages + 1) + 16 + 4 * kBN + 1024;
+};
+
+MOE_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+MOE_DEV void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+MOE_DEV void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+MOE_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+MOE_DEV uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+  return t;
+}
+// Bounded wait: false when the limit expired (the caller records it and drains out).
+MOE_DEV bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - t0 > kWaitLimitNs) return false;
+  return true;
+}
+
+MOE_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+MOE_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+MOE_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+MOE_DEV void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src));
+}
+MOE_DEV void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+MOE_DEV void cp_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes
+// apart (SBO), Blackwell descriptor version 1.
+MOE_DEV uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3fffu);
+  d |= (uint64_t)1 << 16;           // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset
+  d |= (uint64_t)1 << 46;           // version
+  d |= (uint64_t)2 << 61;           // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: bf16 A and B (K-major), fp32 accumulate, M=128.
+MOE_DEV uint32_t idesc_bf16(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+
+MOE_DEV void tc_mma(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(dtmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+MOE_DEV void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
+               : "memory");
+}
+
+MOE_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+
+// bf16 pair (128 + q_j, 128 + q_{j+4}) from nibbles j and j+4 of w.
+MOE_DEV uint32_t nib_pair(uint32_t w, int j) {
+  uint32_t r;
+  const uint32_t v = w >> (4 * j);
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;\n" : "=r"(r) : "r"(v), "r"(0x000f000fu), "r"(0x43004300u));
+  return r;
+}
+
+MOE_DEV uint32_t bf2_sub(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.bf16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+MOE_DEV uint32_t bf2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;\n" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+
+// Eight 4-bit fields of w (element order 0..7) -> eight bf16 values RN(s*q + b), in
+// element order, as four bf16 pairs. s2 / b2 hold (s, s) / (b, b).
+MOE_DEV uint4 dequant8(uint32_t w, uint32_t s2, uint32_t b2) {
+  const uint32_t t0 = nib_pair(w, 0), t1 = nib_pair(w, 1), t2 = nib_pair(w, 2), t3 = nib_pair(w, 3);
+  const uint32_t k128 = 0x43004300u;  // (128, 128)
+  uint4 o;
+  o.x = bf2_fma(bf2_sub(__byte_perm(t0, t1, 0x5410), k128), s2, b2);  // (e0, e1)
+  o.y = bf2_fma(bf2_sub(__byte_perm(t2, t3, 0x5410), k128), s2, b2);  // (e2, e3)
+  o.z = bf2_fma(bf2_sub(__byte_perm(t0, t1, 0x7632), k128), s2, b2);  // (e4, e5)
+  o.w = bf2_fma(bf2_sub(__byte_perm(t2, t3, 0x7632), k128), s2, b2);  // (e6, e7)
+  return o;
+}
+
+// Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled K-major tile.
+MOE_DEV uint32_t sw128_off(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+struct RowMap {
+  int x_mode, x_repeat;
+  const uint32_t* lhs;
+  const uint32_t* perm;
+  MOE_DEV int64_t orig(int64_t pos) const { return perm ? (int64_t)perm[pos] : pos; }
+  MOE_DEV int64_t xrow(int64_t pos) const {
+    if (x_mode == 0) return pos;
+    const int64_t i = orig(pos);
+    return x_mode == 1 ? i / x_repeat : (int64_t)lhs[i];
+  }
+};
+
+}  // namespace
+
+template <bool GATED>
+__global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
+  using C = TcCfg<GATED>;
+  const QgemvArgs& a = ta.q;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar_full = sbase + C::kBarOffset;
+  const uint32_t bar_empty = bar_full + 8 * C::kStages;
+  const uint32_t bar_done = bar_empty + 8 * C::kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kBarOffset + 8 * (2 * C::kStages + 1));
+  int32_t* xrow_s = reinterpret_cast<int32_t*>(smem + C::kBarOffset + 8 * (2 * C::kStages + 1) + 16);
+  __shared__ int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = a.K, N = a.N, G = K >> 6, wpr = K >> 3;
+  const int n0 = blockIdx.x * kBM;
+
+  pdl_wait();
+  // ---- map blockIdx.y to (expert, token tile)
+  const int w = blockIdx.y;
+  int e = 0;
+  int64_t tbeg, tend;
+  if (ta.tile_start) {
+    // tile_start has E + 1 entries: find e with tile_start[e] <= w < tile_start[e + 1]
+    int l = 0, r = ta.num_experts;
+    if (w >= ta.tile_start[r]) return;
+    while (r - l > 1) {
+      const int m = (l + r) >> 1;
+      if (ta.tile_start[m] <= w) l = m;
+      else r = m;
+    }
+    e = l;
+    tbeg = a.offsets[e] + (int64_t)(w - ta.tile_start[e]) * kBN;
+    const int64_t eend = a.offsets[e + 1];
+    tend = (tbeg + kBN < eend) ? tbeg + kBN : eend;
+  } else {
+    tbeg = (int64_t)w * kBN;
+    if (tbeg >= a.n_identity) return;
+    tend = (tbeg + kBN < a.n_identity) ? tbeg + kBN : a.n_identity;
+  }
+  const int ntok = (int)(tend - tbeg);
+  const int nmma = (ntok + 15) & ~15;
+  const RowMap rm{a.x_mode, a.x_repeat, a.lhs, a.perm};
+
+  // ---- setup: barriers, token row indices, TMEM
+  if (tid == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(bar_full + 8 * s, kProducers);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    mbar_init(bar_done, 1);
+  }
+  for (int i = tid; i < kBN; i += kThreads) xrow_s[i] = i < ntok ? (int32_t)rm.xrow(tbeg + i) : -1;
+  if (warp == 4) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < 4) {
+    // ================= producers (then epilogue) =================
+    const int p = tid;                 // 0..127
+    const int half = p & 1;            // which 32 elements of the row's 64
+    const int rsub = p >> 1;           // rows rsub and rsub + 64
+    const uint32_t* wrow[C::kMats][2];
+    const uint16_t* srow[C::kMats][2];
+    const uint16_t* brow[C::kMats][2];
+#pragma unroll
+    for (int m = 0; m < C::kMats; ++m)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const size_t row = (size_t)e * N + n0 + rsub + 64 * i;
+        const uint32_t* W = m ? a.w1 : a.w0;
+        const uint16_t* S = m ? a.s1 : a.s0;
+        const uint16_t* B = m ? a.b1 : a.b0;
+        wrow[m][i] = W + row * wpr + half * 4;
+        srow[m][i] = S + row * G;
+        brow[m][i] = B ? B + row * G : nullptr;
+      }
+    // register ring of packed weights + scales, 2 stages ahead
+    uint4 wr[3][C::kMats][2];
+    uint32_t sr[3][C::kMats][2];  // (s | b << 16)
+    auto load_w = [&](int slot3, int kk) {
+      if (kk < G) {
+#pragma unroll
+        for (int m = 0; m < C::kMats; ++m)
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            wr[slot3][m][i] = __ldg(reinterpret_cast<const uint4*>(wrow[m][i] + (size_t)kk * 8));
+            const uint32_t sv = __ldg(srow[m][i] + kk);
+            const uint32_t bv = brow[m][i] ? __ldg(brow[m][i] + kk) : 0u;
+            sr[slot3][m][i] = sv | (bv << 16);
+          }
+      }
+    };
+    auto issue_b = [&](int kk) {
+      const uint32_t bt = sbase + (kk % C::kStages) * C::kStageBytes + C::kMats * kATileBytes;
+      // 256 rows x 8 chunks; this thread: chunks q = p + 128 i
+#pragma unroll 4
+      for (int i = 0; i < kBN * 8 / kProducers; ++i) {
+        const int q = p + kProducers * i;
+        const int r = q >> 3, c = q & 7;
+        if (r < ntok) cp_async16(bt + sw128_off(r, c), a.x + (size_t)xrow_s[r] * K + kk * kBK + c * 8);
+      }
+      cp_commit();
+    };
+    constexpr int LA = C::kStages - 1;  // B tiles issued this many stages ahead
+    bool ok = true;
+    load_w(0, 0);
+    load_w(1, 1);
+    for (int kk = 0; kk < LA; ++kk) {
+      if (kk < G) {
+        // fresh barriers: the first wait on "empty" passes immediately
+        issue_b(kk);
+      } else {
+        cp_commit();
+      }
+    }
+    for (int kb = 0; kb < G && ok; kb += 3) {
+#pragma unroll
+      for (int r3 = 0; r3 < 3; ++r3) {
+        const int kk = kb + r3;
+        if (kk < G && ok) {
+          const int s = kk % C::kStages;
+          const uint32_t st = sbase + s * C::kStageBytes;
+          // dequantise A(kk) into stage s (freed: its empty barrier was awaited when B(kk) was issued)
+#pragma unroll
+          for (int m = 0; m < C::kMats; ++m)
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const int row = rsub + 64 * i;
+              const uint32_t sv = sr[r3][m][i] & 0xffffu, bv = sr[r3][m][i] >> 16;
+              const uint32_t s2 = sv | (sv << 16), b2 = bv | (bv << 16);
+              const uint4 wv = wr[r3][m][i];
+              const uint32_t ws[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint4 o = dequant8(ws[j], s2, b2);
+                const uint32_t dst = st + m * kATileBytes + sw128_off(row, half * 4 + j);
+                asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(dst), "r"(o.x), "r"(o.y), "r"(o.z),
+                             "r"(o.w)
+                             : "memory");
+              }
+            }
+          load_w((r3 + 2) % 3, kk + 2);
+          // B(kk) landed: at most LA-1 newer groups may still be pending
+          cp_wait<LA - 1>();
+          fence_proxy_async();
+          mbar_arrive(bar_full + 8 * s);
+          // issue B(kk + LA) into the stage MMA(kk + LA - kStages) releases
+          const int kn = kk + LA;
+          if (kn < G) {
+            const int sn = kn % C::kStages;
+            const int use = kn / C::kStages;  // this is use number `use` of stage sn
+            if (use > 0 && !mbar_wait(bar_empty + 8 * sn, (use - 1) & 1)) {
+              ok = false;
+              atomicOr(&abort_flag, 1);
+            }
+            if (ok) issue_b(kn);
+          } else {
+            cp_commit();
+          }
+        }
+      }
+    }
+    cp_wait<0>();
+    // ================= epilogue =================
+    const bool done_ok = __all_sync(0xffffffffu, ok && mbar_wait(bar_done, 0));  // warp-uniform for tcgen05.ld
+    if (!done_ok && lane == 0) atomicOr(&abort_flag, 2);
+    tc_fence_after();
+    pdl_trigger();
+    if (done_ok) {
+      const int row = n0 + 32 * warp + lane;  // TMEM lane = row within the tile
+      const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
+      for (int c0 = 0; c0 < nmma; c0 += 32) {
+        uint32_t g[32];
+        tmem_ld32(tl + c0, g);
+        if (GATED) {
+          uint32_t u[32];
+          tmem_ld32(tl + 256 + c0, u);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int t = c0 + j;
+            if (t < ntok) {
+              const int64_t pos = tbeg + t;
+              const int64_t orow = a.out_mode == 0 ? pos : rm.orig(pos);
+              a.out[(size_t)orow * N + row] = swiglu_bf16(rbf(__uint_as_float(g[j])), rbf(__uint_as_float(u[j])));
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int t = c0 + j;
+            if (t < ntok) {
+              const int64_t pos = tbeg + t;
+              const int64_t orow = a.out_mode == 0 ? pos : rm.orig(pos);
+              a.out[(size_t)orow * N + row] = f2bf(__uint_as_float(g[j]));
+            }
+          }
+        }
+      }
+    }
+  } else if (lane == 0) {
+    // ================= MMA issuer (warp 4, one lane) =================
+    const uint32_t idesc = idesc_bf16(nmma);
+    bool ok = true;
+    for (int kk = 0; kk < G; ++kk) {
+      const int s = kk % C::kStages;
+      if (!mbar_wait(bar_full + 8 * s, (kk / C::kStages) & 1)) {
+        ok = false;
+        atomicOr(&abort_flag, 4);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t st = sbase + s * C::kStageBytes;
+      const uint64_t bdesc = sw128_desc(st + C::kMats * kATileBytes);
+#pragma unroll
+      for (int k16 = 0; k16 < kBK / 16; ++k16) {
+        const uint32_t acc = (kk > 0 || k16 > 0) ? 1u : 0u;
+        const uint64_t koff = (uint64_t)((k16 * 32) >> 4);  // +32 bytes along K
+#pragma unroll
+        for (int m = 0; m < C::kMats; ++m) {
+          const uint64_t adesc = sw128_desc(st + m * kATileBytes);
+          tc_mma(tmem + m * 256, adesc + koff, bdesc + koff, idesc, acc);
+        }
+      }
+      tc_commit(bar_empty + 8 * s);
+    }
+    tc_commit(bar_done);
+    (void)ok;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (abort_flag && tid == 0 && ta.status) atomicOr(ta.status, abort_flag);
+  if (warp == 4) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(C::kTmemCols) : "memory");
+  }
+}
+
+template <bool GATED>
+static cudaError_t launch_tc_t(const TcGemmArgs& a, cudaStream_t st) {
+  using C = TcCfg<GATED>;
+  static thread_local int set_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != set_dev) {
+    cudaError_t err = cudaFuncSetAttribute(tc_gemm_kernel<GATED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           C::kSmemBytes);
+    if (err != cudaSuccess) return err;
+    set_dev = dev;
+  }
+  dim3 grid(a.q.N / kBM, a.max_tiles);
+  return launch_k(tc_gemm_kernel<GATED>, grid, dim3(kThreads), (size_t)C::kSmemBytes, st, a);
+}
+
+cudaError_t launch_tc_gemm(const TcGemmArgs& a, bool gated, cudaStream_t st) {
+  if (a.max_tiles <= 0) return cudaSuccess;
+  if (a.q.N % kBM != 0 || a.q.K % kBK != 0) return cudaErrorInvalidValue;
+  return gated ? launch_tc_t<true>(a, st) : launch_tc_t<false>(a, st);
+}
+
+}  // namespace moe
