@@ -37,6 +37,17 @@ sys.path.insert(0, ROOT)
 METRIC = "MoE-block tokens/s; decode HBM GB/s & prefill TFLOPS vs roofline at 1-8 GPU"
 LAUNCHES_PER_STEP = 6  # router, top-k, grouping (one CTA at this size), gate/up, down, combine
 
+# name -> (config attribute of synth, weight seed, tokens, scoring override, bias std, regime)
+WORKLOADS = {
+    "decode": ("QWEN3_30B_A3B", 1, 64, None, None, "decode"),
+    "prefill": ("QWEN3_30B_A3B", 2, 4096, None, None, "prefill"),
+    "prefill-skewed": ("QWEN3_30B_A3B", 2, 4096, 1, 2.0, "prefill"),
+    "qwen15-prefill": ("QWEN15_MOE_A27B", 0, 512, None, None, "prefill"),
+    "qwen15-decode": ("QWEN15_MOE_A27B", 0, 1, None, None, "decode"),
+    "lfm2-prefill": ("LFM2_8B_A1B", 3, 1024, None, None, "prefill"),
+    "lfm2-decode": ("LFM2_8B_A1B", 3, 1, None, None, "decode"),
+}
+
 
 def parse():
     ap = argparse.ArgumentParser()
@@ -44,7 +55,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS))
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -120,6 +132,21 @@ class ClockSampler:
                 "samples": len(sm), "reasons": sorted(reasons)}
 
 
+def make_workload(args, S):
+    """(config, host weights, tokens per GPU, regime) of the selected workload."""
+    from dataclasses import replace
+    name, seed, T, scoring, bias_std, regime = WORKLOADS[args.workload]
+    cfg = getattr(S, name)
+    if scoring is not None:
+        cfg = replace(cfg, scoring=scoring)
+    bw = S.host_block(cfg, seed)
+    if scoring is not None and bias_std is not None:
+        bw = S.with_scoring(bw, scoring, seed, bias_std)
+    if args.tokens:
+        T = args.tokens
+    return bw.config, bw, T, regime
+
+
 def reference_arm(args):
     """The CPU oracle on this host's cores (rank 0 only)."""
     rank = int(os.environ.get("RANK", "0"))
@@ -128,10 +155,11 @@ def reference_arm(args):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     import mlx_rs_b200.synth as S
-    cfg = S.QWEN3_30B_A3B
-    T = args.tokens
-    bw = S.host_block(cfg, 1)
-    xs = [S.host_x(1000 + i, T, cfg.hidden) for i in range(4)]
+    cfg, bw, T, regime = make_workload(args, S)
+    # prefill: each step times a bounded sample of the batch (rows of the block are
+    # independent, so the per-token rate of a sample is the rate of the batch)
+    Ts = min(T, 128) if regime == "prefill" else T
+    xs = [S.host_x(1000 + i, Ts, cfg.hidden) for i in range(4)]
     cores = os.cpu_count() or 1
     for i in range(max(1, min(args.warmup, 2))):
         O.block_forward(bw, xs[i % 4], nthreads=cores)
@@ -141,16 +169,16 @@ def reference_arm(args):
         O.block_forward(bw, xs[i % 4], nthreads=cores)
         times.append(time.perf_counter() - t0)
     ms = 1e3 * statistics.mean(times)
-    value = T / (ms / 1e3)
+    value = Ts / (ms / 1e3)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"{cfg.name} MoE block decode, T={T} tokens", "global_batch": T,
+        "config": {"workload": f"{cfg.name} MoE block {regime}, T={T} tokens", "global_batch": T,
                    "parallelism": "cpu"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} block calls of T={T} tokens (CPU oracle, C restatement "
-                                   f"of the reference block; MLX itself is not available)"},
+                         "sample": f"{args.steps} block calls of {Ts} of the T={T} tokens (CPU oracle, C "
+                                   f"restatement of the reference block; MLX itself is not available)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -197,10 +225,9 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    cfg = S.QWEN3_30B_A3B
-    T, H = args.tokens, cfg.hidden
-    bw_host = S.host_block(cfg, 1)
-    blk = SparseMoeBlock(S.to_device(bw_host, dev))
+    cfg, bw_host, T, regime = make_workload(args, S)
+    H = cfg.hidden
+    blk = SparseMoeBlock(S.to_device(bw_host, dev), cfg)
     pool = 8
     xs_host = [S.host_x(1000 + 97 * rank + i, T, H) for i in range(pool)]
     xs = [S.x_to_device(x, dev) for x in xs_host]
@@ -310,10 +337,26 @@ def main():
         "down": U * per_mat + T * cfg.top_k * cfg.moe_inter * 2,
         "router": wb["router"] + T * H * 2,
     }
+    P = T * cfg.top_k
+    flops = {"gate_up": 2.0 * P * 2 * H * cfg.moe_inter, "down": 2.0 * P * H * cfg.moe_inter}
     dom = max(("gate_up", "down"), key=lambda kname: stage_ms[kname])
     hbm, tf, peak_kind = measured_peaks()
-    achieved = alg[dom] / (stage_ms[dom] / 1e3) / 1e9
     block_bytes = alg["gate_up"] + alg["down"] + alg["router"]
+    if regime == "prefill":
+        kind = "tcgen05 grouped GEMM" if T * cfg.top_k >= 32 * cfg.num_experts else "qgemv"
+        achieved = flops[dom] / (stage_ms[dom] / 1e3) / 1e12
+        roof = {"bound": "tensor", "kernel": f"{kind} {dom}", "achieved": achieved, "peak": tf, "unit": "TFLOP/s",
+                "frac": achieved / tf, "peak_kind": f"{peak_kind} bf16 burst", "traffic": None,
+                "algorithmic_flops_per_launch": flops[dom], "launch_ms": stage_ms[dom],
+                "block_TFLOPs": (flops["gate_up"] + flops["down"]) / (ms / 1e3) / 1e12, "stage_ms": stage_ms}
+    else:
+        achieved = alg[dom] / (stage_ms[dom] / 1e3) / 1e9
+        roof = {"bound": "hbm", "kernel": f"qgemv {dom}", "achieved": achieved, "peak": hbm,
+                "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind,
+                "frac_of_8TBps_spec": achieved / 8000.0, "traffic": None,
+                "algorithmic_bytes_per_launch": alg[dom], "launch_ms": stage_ms[dom],
+                "block_algorithmic_GBps": block_bytes / (ms / 1e3) / 1e9,
+                "stage_ms": stage_ms}
 
     # ---- e2e through the public API from pinned host memory
     xs_pin = [torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).pin_memory() for x in xs_host]
@@ -338,7 +381,7 @@ def main():
         e2e = float(t.item())
 
     sweep = {}
-    if not args.no_sweep and rank == 0 and world == 1:
+    if not args.no_sweep and rank == 0 and world == 1 and regime == "decode" and args.workload == "decode":
         for Ts in (1, 8, 32, 64):
             xsw = [S.device_x(77 + i, Ts, H, dev) for i in range(4)]
             o = torch.empty(Ts, H, dtype=torch.bfloat16, device=dev)
@@ -361,7 +404,11 @@ def main():
                                "stage_us": {kk: round(vv * 1e3, 2) for kk, vv in st.items()},
                                "block_GBps": bytes_ / (statistics.median(tms) / 1e3) / 1e9}
 
-    cpu = cpu_baseline(bw_host, xs_host[0], args.cpu_seconds) if (rank == 0 and world == 1) else None
+    cpu = None
+    if rank == 0 and world == 1:
+        cpu = cpu_baseline(bw_host, xs_host[0][: min(T, 128)], args.cpu_seconds)
+        if T > 128:
+            cpu["sample"] += f" ({min(T, 128)} of the {T} tokens; rows are independent)"
     if world > 1:
         torch.cuda.synchronize()
         dist.barrier()
@@ -370,18 +417,13 @@ def main():
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"{cfg.name} MoE block decode, T={T} tokens per GPU", "global_batch": T * world,
+            "config": {"workload": f"{cfg.name} MoE block {regime}, T={T} tokens per GPU", "global_batch": T * world,
                        "seq_len": 1, "parallelism": f"replicas{world}" if world > 1 else "single",
                        "experts": cfg.num_experts, "top_k": cfg.top_k, "hidden": H, "moe_inter": cfg.moe_inter,
                        "l2": "flushed (256 MiB write) before every timed step", "launch": mode,
                        "clock_window": "nvidia-smi every 200 ms across 0.6 s of untimed steps, the timed steps, 0.6 s more",
                        "distinct_experts_per_step": U, "sweep_eager": sweep},
-            "roofline": {"bound": "hbm", "kernel": f"qgemv {dom}", "achieved": achieved, "peak": hbm,
-                         "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind,
-                         "frac_of_8TBps_spec": achieved / 8000.0, "traffic": None,
-                         "algorithmic_bytes_per_launch": alg[dom], "launch_ms": stage_ms[dom],
-                         "block_algorithmic_GBps": block_bytes / (ms / 1e3) / 1e9,
-                         "stage_ms": stage_ms},
+            "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": {"value": world * T / (e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
                     "d2h_bytes_per_step": T * H * 2, "ms_per_step": e2e},
