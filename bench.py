@@ -1,23 +1,29 @@
 """Benchmark of the B200 MoE block (one JSON line on rank 0).
 
-Workload (N=1): one Qwen3-30B-A3B-shaped MoE block (hidden 2048, 128 experts, top-8,
-moe_intermediate 768, softmax + top-k renormalisation, 4-bit affine group-64 weights),
-decode batch T=64 tokens; synthetic seeded weights and activations with the benchmark
-distributions. A step = one block forward over one batch of T tokens; every step uses a
-different token batch, and L2 is flushed (a 256 MiB write) before each timed step.
+Default workload (N=1): one Qwen3-30B-A3B-shaped MoE block (hidden 2048, 128 experts,
+top-8, moe_intermediate 768, softmax + top-k renormalisation, 4-bit affine group-64
+weights), decode batch T=64 tokens; synthetic seeded weights and activations with the
+benchmark distributions. A step = one block forward over one batch of T tokens; every
+step uses a different token batch, and L2 is flushed (a 256 MiB write) before each
+timed step.
 
   value  tokens/s, device-timed with CUDA events on the launching stream, inputs
-         resident in HBM, block replayed from a CUDA graph (max over ranks)
-  e2e    tokens/s through the public API (SparseMoeBlock.forward) from pinned host
-         memory: H2D copy of x, block, D2H copy of the output, per step
+         resident in HBM (max over ranks)
+  e2e    tokens/s through the public API (SparseMoeBlock.forward, or
+         ExpertParallelBlock.forward under torchrun) from pinned host memory: H2D copy
+         of x, block, D2H copy of the output, per step
   roofline  the dominant kernel (largest per-stage device time) against the measured
-         HBM copy bandwidth, algorithmic bytes = distinct experts actually selected x
-         bytes per expert matrix
+         HBM copy bandwidth (decode) or bf16 tensor peak (prefill)
   cpu_baseline  the CPU oracle (C restatement of the reference block) on the host cores
 
---gpus N (under torchrun) runs N ranks; each rank owns T tokens and a full replica of
-the block (no data-path collective; weak scaling). --impl reference times the CPU
-oracle only (rank 0).
+--gpus N (under torchrun, one rank per GPU): expert parallelism. Rank r owns experts
+[r*E/N, (r+1)*E/N) and its own T tokens (weak scaling: 64 decode tokens per GPU); the
+token rows are all-gathered and the fp32 partial outputs returned with an all-to-all
+over NCCL (mlx_rs_b200.ep).
+--workload stack-prefill / stack-decode: the 48-block Qwen3-30B-A3B stack with an
+RMSNorm between blocks, 8192 / 256 tokens in total split over the N ranks (strong
+scaling), expert-parallel for N > 1.
+--impl reference times the CPU oracle only (rank 0).
 """
 from __future__ import annotations
 
@@ -37,15 +43,18 @@ sys.path.insert(0, ROOT)
 METRIC = "MoE-block tokens/s; decode HBM GB/s & prefill TFLOPS vs roofline at 1-8 GPU"
 LAUNCHES_PER_STEP = 6  # router, top-k, grouping (one CTA at this size), gate/up, down, combine
 
-# name -> (config attribute of synth, weight seed, tokens, scoring override, bias std, regime)
+# name -> (config attribute of synth, weight seed, tokens, scoring override, bias std, regime, blocks)
+# Single blocks: tokens per GPU. Stacks: tokens in total, split over the GPUs.
 WORKLOADS = {
-    "decode": ("QWEN3_30B_A3B", 1, 64, None, None, "decode"),
-    "prefill": ("QWEN3_30B_A3B", 2, 4096, None, None, "prefill"),
-    "prefill-skewed": ("QWEN3_30B_A3B", 2, 4096, 1, 2.0, "prefill"),
-    "qwen15-prefill": ("QWEN15_MOE_A27B", 0, 512, None, None, "prefill"),
-    "qwen15-decode": ("QWEN15_MOE_A27B", 0, 1, None, None, "decode"),
-    "lfm2-prefill": ("LFM2_8B_A1B", 3, 1024, None, None, "prefill"),
-    "lfm2-decode": ("LFM2_8B_A1B", 3, 1, None, None, "decode"),
+    "decode": ("QWEN3_30B_A3B", 1, 64, None, None, "decode", 1),
+    "prefill": ("QWEN3_30B_A3B", 2, 4096, None, None, "prefill", 1),
+    "prefill-skewed": ("QWEN3_30B_A3B", 2, 4096, 1, 2.0, "prefill", 1),
+    "qwen15-prefill": ("QWEN15_MOE_A27B", 0, 512, None, None, "prefill", 1),
+    "qwen15-decode": ("QWEN15_MOE_A27B", 0, 1, None, None, "decode", 1),
+    "lfm2-prefill": ("LFM2_8B_A1B", 3, 1024, None, None, "prefill", 1),
+    "lfm2-decode": ("LFM2_8B_A1B", 3, 1, None, None, "decode", 1),
+    "stack-prefill": ("QWEN3_30B_A3B", 4, 8192, None, None, "prefill", 48),
+    "stack-decode": ("QWEN3_30B_A3B", 4, 256, None, None, "decode", 48),
 }
 
 
@@ -132,19 +141,22 @@ class ClockSampler:
                 "samples": len(sm), "reasons": sorted(reasons)}
 
 
-def make_workload(args, S):
-    """(config, host weights, tokens per GPU, regime) of the selected workload."""
+def make_workload(args, S, host=True):
+    """(config, host weights of block 0 or None, tokens, regime, blocks) of the workload."""
     from dataclasses import replace
-    name, seed, T, scoring, bias_std, regime = WORKLOADS[args.workload]
+    name, seed, T, scoring, bias_std, regime, layers = WORKLOADS[args.workload]
     cfg = getattr(S, name)
     if scoring is not None:
         cfg = replace(cfg, scoring=scoring)
-    bw = S.host_block(cfg, seed)
-    if scoring is not None and bias_std is not None:
-        bw = S.with_scoring(bw, scoring, seed, bias_std)
+    bw = None
+    if host:
+        bw = S.host_block(cfg, seed)
+        if scoring is not None and bias_std is not None:
+            bw = S.with_scoring(bw, scoring, seed, bias_std)
+        cfg = bw.config
     if args.tokens:
         T = args.tokens
-    return bw.config, bw, T, regime
+    return cfg, bw, T, regime, layers
 
 
 def reference_arm(args):
@@ -155,10 +167,12 @@ def reference_arm(args):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     import mlx_rs_b200.synth as S
-    cfg, bw, T, regime = make_workload(args, S)
-    # prefill: each step times a bounded sample of the batch (rows of the block are
-    # independent, so the per-token rate of a sample is the rate of the batch)
-    Ts = min(T, 128) if regime == "prefill" else T
+    cfg, bw, T, regime, layers = make_workload(args, S)
+    world = args.gpus
+    # each step times a bounded sample of one block's tokens (rows of the block are
+    # independent, so the per-token rate of a sample is the rate of the batch); a
+    # stack's rate is the block rate divided by its number of blocks
+    Ts = min(T, 128) if regime == "prefill" or layers > 1 else T
     xs = [S.host_x(1000 + i, Ts, cfg.hidden) for i in range(4)]
     cores = os.cpu_count() or 1
     for i in range(max(1, min(args.warmup, 2))):
@@ -168,17 +182,19 @@ def reference_arm(args):
         t0 = time.perf_counter()
         O.block_forward(bw, xs[i % 4], nthreads=cores)
         times.append(time.perf_counter() - t0)
-    ms = 1e3 * statistics.mean(times)
+    ms = 1e3 * statistics.mean(times) * layers
     value = Ts / (ms / 1e3)
+    what = f"{layers}-block stack" if layers > 1 else "MoE block"
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"{cfg.name} MoE block {regime}, T={T} tokens", "global_batch": T,
+        "scaling": "strong" if layers > 1 else "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{cfg.name} {what} {regime}, T={T} tokens", "global_batch": T,
                    "parallelism": "cpu"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"{args.steps} block calls of {Ts} of the T={T} tokens (CPU oracle, C "
-                                   f"restatement of the reference block; MLX itself is not available)"},
+                                   f"restatement of the reference block; MLX itself is not available)"
+                                   + (f"; rate divided by the {layers} blocks" if layers > 1 else "")},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -203,18 +219,136 @@ def cpu_baseline(bw_host, x_host, seconds):
                       f"reference block), median"}
 
 
+class Timer:
+    """Warm-up, clock sampling window and the timed steps of one bench run.
+
+    step(i) enqueues step i bracketed by two CUDA events on the launching stream and
+    returns them. nvidia-smi samples every 200 ms, longer than short steps take, so the
+    sampler runs across a window of back-to-back (untimed) steps that brackets the timed
+    ones. Returns the mean step time in ms (max over ranks) and the clock record."""
+
+    def __init__(self, args, world, local, dev):
+        self.args, self.world, self.local, self.dev = args, world, local, dev
+
+    def _barrier(self):
+        import torch
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def _busy_rounds(self, step, seconds=0.6):
+        """Rounds of 4 back-to-back steps that fill `seconds`, agreed by all ranks (every
+        rank must run the same number of steps: they hold collectives)."""
+        import torch
+        import torch.distributed as dist
+        t0 = time.perf_counter()
+        for i in range(4):
+            step(i)
+        torch.cuda.synchronize()
+        dt = max(time.perf_counter() - t0, 1e-6)
+        n = max(1, int(seconds / dt + 0.999))
+        if self.world > 1:
+            t = torch.tensor([n], device=self.dev, dtype=torch.int64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            n = int(t.item())
+        return n
+
+    def _busy(self, step, n):
+        import torch
+        for _ in range(n):
+            for i in range(4):
+                step(i)
+        torch.cuda.synchronize()
+
+    def run(self, step):
+        for i in range(max(3, self.args.warmup)):
+            step(i)
+        self._barrier()
+        n = self._busy_rounds(step)
+        self._barrier()
+        clocks = ClockSampler(self.local)
+        clocks.start()
+        clocks.wait_first_sample()
+        self._busy(step, n)
+        self._barrier()
+        evs = [step(i) for i in range(self.args.steps)]
+        self._barrier()
+        self._busy(step, n)
+        self._barrier()
+        clock_info = clocks.stop()
+        ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        return self.max_over_ranks(ms), clock_info
+
+    def max_over_ranks(self, v):
+        import torch
+        import torch.distributed as dist
+        if self.world == 1:
+            return v
+        t = torch.tensor([v], device=self.dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+
+def events():
+    import torch
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def e2e_run(args, fwd, xs_host_bits, out_shape, dev, timer):
+    """Mean ms of H2D (pinned) + forward + D2H per step, max over ranks."""
+    import numpy as np
+    import torch
+    stream = torch.cuda.current_stream(dev)
+    xs_pin = [torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).pin_memory() for x in xs_host_bits]
+    out_pin = torch.empty(*out_shape, dtype=torch.bfloat16).pin_memory()
+    xdev = torch.empty(xs_pin[0].shape, dtype=torch.bfloat16, device=dev)
+    times = []
+    for i in range(args.warmup + args.steps):
+        a, b = events()
+        a.record(stream)
+        xdev.copy_(xs_pin[i % len(xs_pin)], non_blocking=True)
+        y = fwd(xdev)
+        out_pin.copy_(y, non_blocking=True)
+        b.record(stream)
+        b.synchronize()
+        if i >= args.warmup:
+            times.append(a.elapsed_time(b))
+    return timer.max_over_ranks(statistics.mean(times))
+
+
+def hbm_roofline(name, alg_bytes, launch_ms, extra=None):
+    hbm, _, peak_kind = measured_peaks()
+    achieved = alg_bytes / (launch_ms / 1e3) / 1e9
+    r = {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+         "peak_kind": peak_kind, "frac_of_8TBps_spec": achieved / 8000.0, "traffic": None,
+         "algorithmic_bytes_per_launch": alg_bytes, "launch_ms": launch_ms}
+    r.update(extra or {})
+    return r
+
+
+def tensor_roofline(name, flops, launch_ms, extra=None):
+    _, tf, peak_kind = measured_peaks()
+    achieved = flops / (launch_ms / 1e3) / 1e12
+    r = {"bound": "tensor", "kernel": name, "achieved": achieved, "peak": tf, "unit": "TFLOP/s",
+         "frac": achieved / tf, "peak_kind": f"{peak_kind} bf16 burst", "traffic": None,
+         "algorithmic_flops_per_launch": flops, "launch_ms": launch_ms}
+    r.update(extra or {})
+    return r
+
+
+def group_launches(P, E):
+    return 1 if (P <= 32768 and E <= 512) else 3
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
         return
-    import numpy as np
     import torch
     import torch.distributed as dist
-
-    import mlx_rs_b200
-    import mlx_rs_b200.synth as S
-    from mlx_rs_b200.block import SparseMoeBlock
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -224,12 +358,36 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        if WORKLOADS[args.workload][6] > 1:
+            line = run_stack(args, world, rank, local, dev)
+        elif world > 1:
+            line = run_ep_block(args, world, rank, local, dev)
+        else:
+            line = run_block(args, dev)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            torch.cuda.synchronize()
+            dist.barrier()
+            dist.destroy_process_group()
 
-    cfg, bw_host, T, regime = make_workload(args, S)
+
+def run_block(args, dev):
+    """One GPU, one block: device time from a CUDA graph, stage profile, e2e, sweep."""
+    import numpy as np
+    import torch
+
+    import mlx_rs_b200
+    import mlx_rs_b200.synth as S
+    from mlx_rs_b200.block import SparseMoeBlock
+
+    cfg, bw_host, T, regime, _ = make_workload(args, S)
     H = cfg.hidden
     blk = SparseMoeBlock(S.to_device(bw_host, dev), cfg)
     pool = 8
-    xs_host = [S.host_x(1000 + 97 * rank + i, T, H) for i in range(pool)]
+    xs_host = [S.host_x(1000 + i, T, H) for i in range(pool)]
     xs = [S.x_to_device(x, dev) for x in xs_host]
     blk.reserve(max(T, 64))
     out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
@@ -265,60 +423,23 @@ def main():
             torch.cuda.synchronize()
 
     def step(i):
+        a, b = events()
         if graph is not None:
             static_x.copy_(xs[i % pool])
             flush.zero_()
-            a = torch.cuda.Event(enable_timing=True)
-            b = torch.cuda.Event(enable_timing=True)
             a.record(stream)
             graph.replay()
             b.record(stream)
             return a, b
         flush.zero_()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
         blk.forward(xs[i % pool], out)
         b.record(stream)
         return a, b
 
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    # nvidia-smi samples every 200 ms, longer than the timed steps take, so the sampler
-    # runs across a window of back-to-back (untimed) steps that brackets the timed ones.
-    clocks = ClockSampler(local)
-    clocks.start()
-    clocks.wait_first_sample()
-    t_busy = time.perf_counter() + 0.6
-    while time.perf_counter() < t_busy:
-        for i in range(8):
-            step(i)
-        torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    evs = [step(i) for i in range(args.steps)]
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    t_busy = time.perf_counter() + 0.6
-    while time.perf_counter() < t_busy:
-        for i in range(8):
-            step(i)
-        torch.cuda.synchronize()
-    clock_info = clocks.stop()
-    step_ms = [a.elapsed_time(b) for a, b in evs]
-    ms = statistics.mean(step_ms)
-    if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    value = world * T / (ms / 1e3)
+    timer = Timer(args, 1, int(dev.index), dev)
+    ms, clock_info = timer.run(step)
+    value = T / (ms / 1e3)
 
     # ---- per-stage device times (profile entry point) for the roofline
     stage_acc, n_act = {}, []
@@ -340,48 +461,20 @@ def main():
     P = T * cfg.top_k
     flops = {"gate_up": 2.0 * P * 2 * H * cfg.moe_inter, "down": 2.0 * P * H * cfg.moe_inter}
     dom = max(("gate_up", "down"), key=lambda kname: stage_ms[kname])
-    hbm, tf, peak_kind = measured_peaks()
     block_bytes = alg["gate_up"] + alg["down"] + alg["router"]
     if regime == "prefill":
-        kind = "tcgen05 grouped GEMM" if T * cfg.top_k >= 32 * cfg.num_experts else "qgemv"
-        achieved = flops[dom] / (stage_ms[dom] / 1e3) / 1e12
-        roof = {"bound": "tensor", "kernel": f"{kind} {dom}", "achieved": achieved, "peak": tf, "unit": "TFLOP/s",
-                "frac": achieved / tf, "peak_kind": f"{peak_kind} bf16 burst", "traffic": None,
-                "algorithmic_flops_per_launch": flops[dom], "launch_ms": stage_ms[dom],
-                "block_TFLOPs": (flops["gate_up"] + flops["down"]) / (ms / 1e3) / 1e12, "stage_ms": stage_ms}
+        kind = "tcgen05 grouped GEMM" if P >= 32 * cfg.num_experts else "qgemv"
+        roof = tensor_roofline(f"{kind} {dom}", flops[dom], stage_ms[dom],
+                               {"block_TFLOPs": (flops["gate_up"] + flops["down"]) / (ms / 1e3) / 1e12,
+                                "stage_ms": stage_ms})
     else:
-        achieved = alg[dom] / (stage_ms[dom] / 1e3) / 1e9
-        roof = {"bound": "hbm", "kernel": f"qgemv {dom}", "achieved": achieved, "peak": hbm,
-                "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind,
-                "frac_of_8TBps_spec": achieved / 8000.0, "traffic": None,
-                "algorithmic_bytes_per_launch": alg[dom], "launch_ms": stage_ms[dom],
-                "block_algorithmic_GBps": block_bytes / (ms / 1e3) / 1e9,
-                "stage_ms": stage_ms}
+        roof = hbm_roofline(f"qgemv {dom}", alg[dom], stage_ms[dom],
+                            {"block_algorithmic_GBps": block_bytes / (ms / 1e3) / 1e9, "stage_ms": stage_ms})
 
-    # ---- e2e through the public API from pinned host memory
-    xs_pin = [torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).pin_memory() for x in xs_host]
-    out_pin = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
-    xdev = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
-    e2e_ms = []
-    for i in range(args.warmup + args.steps):
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        xdev.copy_(xs_pin[i % pool], non_blocking=True)
-        y = blk.forward(xdev, out)
-        out_pin.copy_(y, non_blocking=True)
-        b.record(stream)
-        b.synchronize()
-        if i >= args.warmup:
-            e2e_ms.append(a.elapsed_time(b))
-    e2e = statistics.mean(e2e_ms)
-    if world > 1:
-        t = torch.tensor([e2e], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e = float(t.item())
+    e2e = e2e_run(args, lambda xd: blk.forward(xd, out), xs_host, (T, H), dev, timer)
 
     sweep = {}
-    if not args.no_sweep and rank == 0 and world == 1 and regime == "decode" and args.workload == "decode":
+    if not args.no_sweep and regime == "decode" and args.workload == "decode":
         for Ts in (1, 8, 32, 64):
             xsw = [S.device_x(77 + i, Ts, H, dev) for i in range(4)]
             o = torch.empty(Ts, H, dtype=torch.bfloat16, device=dev)
@@ -390,8 +483,7 @@ def main():
             tms = []
             for i in range(10):
                 flush.zero_()
-                a = torch.cuda.Event(enable_timing=True)
-                b = torch.cuda.Event(enable_timing=True)
+                a, b = events()
                 a.record(stream)
                 blk.forward(xsw[i % 4], o)
                 b.record(stream)
@@ -404,37 +496,261 @@ def main():
                                "stage_us": {kk: round(vv * 1e3, 2) for kk, vv in st.items()},
                                "block_GBps": bytes_ / (statistics.median(tms) / 1e3) / 1e9}
 
+    cpu = cpu_baseline(bw_host, xs_host[0][: min(T, 128)], args.cpu_seconds)
+    if T > 128:
+        cpu["sample"] += f" ({min(T, 128)} of the {T} tokens; rows are independent)"
+    launches = 5 + group_launches(P, cfg.num_experts) + (2 if cfg.shared_inter else 0)
+    return {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{cfg.name} MoE block {regime}, T={T} tokens per GPU", "global_batch": T,
+                   "seq_len": 1, "parallelism": "single",
+                   "experts": cfg.num_experts, "top_k": cfg.top_k, "hidden": H, "moe_inter": cfg.moe_inter,
+                   "l2": "flushed (256 MiB write) before every timed step", "launch": mode,
+                   "clock_window": "nvidia-smi every 200 ms across 0.6 s of untimed steps, the timed steps, 0.6 s more",
+                   "distinct_experts_per_step": U, "sweep_eager": sweep},
+        "roofline": roof,
+        "cpu_baseline": cpu,
+        "e2e": {"value": T / (e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2, "ms_per_step": e2e},
+        "gpu_launches": launches * args.steps,
+        "clocks": clock_info,
+        "library": mlx_rs_b200.library_path,
+    }
+
+
+def ep_stage_times(blk, x, dev, world, reps=6):
+    """Device time of each step of an expert-parallel block (route, the two all-gathers,
+    experts, the all-to-all, finish), from CUDA events between the steps."""
+    import torch
+    import torch.distributed as dist
+    b = blk.buffers(x.shape[0], dev)
+    out = torch.empty_like(x)
+    names = ("route", "all_gather", "experts", "all_to_all", "finish")
+    acc = {n: [] for n in names}
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(reps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+        ev[0].record(stream)
+        blk.ops.route(blk.bound, x, b.packed)
+        ev[1].record(stream)
+        dist.all_gather_into_tensor(b.x_all.view(torch.uint8), x.view(torch.uint8))
+        dist.all_gather_into_tensor(b.packed_all, b.packed)
+        ev[2].record(stream)
+        blk.ops.experts(blk.bound, b.x_all, b.packed_all, blk.expert_begin, blk.num_local, b.partial)
+        ev[3].record(stream)
+        dist.all_to_all_single(b.received.view(-1), b.partial.view(-1))
+        ev[4].record(stream)
+        blk.ops.finish(b.received, world, out)
+        ev[5].record(stream)
+        torch.cuda.synchronize()
+        for i, n in enumerate(names):
+            acc[n].append(ev[i].elapsed_time(ev[i + 1]))
+    return {n: statistics.median(v) for n, v in acc.items()}, b
+
+
+def local_active_experts(b, e0, n):
+    import numpy as np
+    pk = b.packed_all.cpu().numpy().view(np.uint32) & 0xFFFF
+    loc = pk[(pk >= e0) & (pk < e0 + n)]
+    return int(np.unique(loc).size), int(loc.size)
+
+
+def run_ep_block(args, world, rank, local, dev):
+    """N ranks, one block, expert-parallel; each rank brings its own T tokens."""
+    import torch
+
+    import mlx_rs_b200
+    import mlx_rs_b200.synth as S
+    from mlx_rs_b200.ep import ExpertParallelBlock, expert_range, local_weights
+
+    cfg, bw_host, T, regime, _ = make_workload(args, S)
+    H = cfg.hidden
+    e0, n = expert_range(cfg.num_experts, world, rank)
+    blk = ExpertParallelBlock(local_weights(S.to_device(bw_host, dev), e0, n), cfg, expert_begin=e0, num_local=n)
+    del bw_host
+    pool = 8
+    xs_host = [S.host_x(1000 + 97 * rank + i, T, H) for i in range(pool)]
+    xs = [S.x_to_device(x, dev) for x in xs_host]
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        a, b = events()
+        flush.zero_()
+        a.record(stream)
+        blk.forward(xs[i % pool], out)
+        b.record(stream)
+        return a, b
+
+    timer = Timer(args, world, local, dev)
+    ms, clock_info = timer.run(step)
+    value = world * T / (ms / 1e3)
+
+    stage_ms, buf = ep_stage_times(blk, xs[0], dev, world)
+    n_act, n_pairs = local_active_experts(buf, e0, n)
+    wb = S.weight_bytes(cfg)
+    P_all = world * T * cfg.top_k
+    flops = 2.0 * n_pairs * 3 * H * cfg.moe_inter
+    if regime == "prefill":
+        roof = tensor_roofline("ep experts (gate/up + down)", flops, stage_ms["experts"], {"stage_ms": stage_ms})
+    else:
+        roof = hbm_roofline("ep experts (gate/up + down)", n_act * wb["per_expert"], stage_ms["experts"],
+                            {"stage_ms": stage_ms, "local_experts_touched": n_act})
+    roof["rank"] = 0  # rank 0's own experts and their device time
+    e2e = e2e_run(args, lambda xd: blk.forward(xd, out), xs_host, (T, H), dev, timer)
+    launches = 4 + 2 + group_launches(P_all, n)
+    return {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{cfg.name} MoE block {regime}, T={T} tokens per GPU, expert-parallel",
+                   "global_batch": T * world, "seq_len": 1, "parallelism": f"ep{world}",
+                   "experts": cfg.num_experts, "experts_per_gpu": n, "top_k": cfg.top_k, "hidden": H,
+                   "moe_inter": cfg.moe_inter, "collectives": "NCCL all_gather x2 (dispatch), all_to_all (combine)",
+                   "l2": "flushed (256 MiB write) before every timed step", "launch": "eager",
+                   "clock_window": "nvidia-smi every 200 ms across 0.6 s of untimed steps, the timed steps, 0.6 s more"},
+        "roofline": roof,
+        "cpu_baseline": None,
+        "e2e": {"value": world * T / (e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2, "ms_per_step": e2e},
+        "gpu_launches": launches * args.steps,
+        "clocks": clock_info,
+        "library": mlx_rs_b200.library_path,
+    }
+
+
+def run_stack(args, world, rank, local, dev):
+    """The 48-block stack, T tokens in total over the N ranks (strong scaling)."""
+    import numpy as np
+    import torch
+
+    import mlx_rs_b200
+    import mlx_rs_b200.synth as S
+    from mlx_rs_b200.block import MoeStack, RmsNorm, SparseMoeBlock
+    from mlx_rs_b200.ep import ExpertParallelBlock, ExpertParallelStack, expert_range, local_weights
+
+    cfg, _, T, regime, layers = make_workload(args, S, host=False)
+    seed = WORKLOADS[args.workload][1]
+    H = cfg.hidden
+    if T % world:
+        raise SystemExit(f"{T} tokens do not split over {world} ranks")
+    T_r = T // world
+    e0, n = expert_range(cfg.num_experts, world, rank)
+    ones = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    blocks = []
+    for l in range(layers):
+        bw = S.device_block(cfg, seed * 1000 + l, dev)  # identical on every rank
+        if world > 1:
+            blocks.append(ExpertParallelBlock(local_weights(bw, e0, n), cfg, expert_begin=e0, num_local=n))
+        else:
+            blocks.append(SparseMoeBlock(bw, cfg))
+        del bw
+    torch.cuda.empty_cache()
+    if world > 1:
+        stack = ExpertParallelStack(blocks, [None] + [ones] * (layers - 1))
+    else:
+        for b in blocks:
+            b.reserve(T)
+        stack = MoeStack(blocks, [None] + [RmsNorm(ones, 1e-6)] * (layers - 1))
+    pool = 4
+    xs = [S.device_x(seed * 7 + i, T, H, dev)[rank * T_r:(rank + 1) * T_r].contiguous() for i in range(pool)]
+    out = torch.empty(T_r, H, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def fwd(x):
+        return stack.forward(x, out) if world > 1 else out.copy_(stack.forward(x))
+
+    # one GPU: the whole stack replays from a CUDA graph; expert-parallel: eager launches
+    graph, mode = None, "eager"
+    static_x = torch.empty_like(xs[0])
+    if world == 1 and not args.no_graph:
+        try:
+            for i in range(2):
+                fwd(xs[i])
+            torch.cuda.synchronize()
+            static_x.copy_(xs[0])
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                fwd(static_x)
+            graph.replay()
+            torch.cuda.synchronize()
+            mode = "cuda_graph"
+        except Exception as e:
+            graph, mode = None, f"eager (graph capture failed: {type(e).__name__})"
+            torch.cuda.synchronize()
+
+    def step(i):
+        a, b = events()
+        if graph is not None:
+            static_x.copy_(xs[i % pool])
+            a.record(stream)
+            graph.replay()
+            b.record(stream)
+            return a, b
+        a.record(stream)
+        fwd(xs[i % pool])
+        b.record(stream)
+        return a, b
+
+    timer = Timer(args, world, local, dev)
+    ms, clock_info = timer.run(step)
+    value = T / (ms / 1e3)
+
+    # roofline: the dominant kernel of one block of this rank's share
+    wb = S.weight_bytes(cfg)
+    if world > 1:
+        stage_ms, buf = ep_stage_times(blocks[0], xs[0], dev, world)
+        n_act, n_pairs = local_active_experts(buf, e0, n)
+        flops = 2.0 * n_pairs * 3 * H * cfg.moe_inter
+        kname, launch_ms, bytes_ = "ep experts (gate/up + down)", stage_ms["experts"], n_act * wb["per_expert"]
+    else:
+        _, stage_ms, n_act = blocks[0].profile(xs[0])
+        P = T * cfg.top_k
+        dom = max(("gate_up", "down"), key=lambda k: stage_ms[k])
+        mats = 2 if dom == "gate_up" else 1
+        flops = 2.0 * P * mats * H * cfg.moe_inter
+        bytes_ = n_act * wb["per_expert"] * mats / 3
+        kname = f"{'tcgen05 grouped GEMM' if P >= 32 * cfg.num_experts else 'qgemv'} {dom}"
+        launch_ms = stage_ms[dom]
+    extra = {"stage_ms_block0": stage_ms, "stack_ms": ms, "rank": 0}
+    if regime == "prefill":
+        roof = tensor_roofline(kname, flops, launch_ms, extra)
+    else:
+        roof = hbm_roofline(kname, bytes_, launch_ms, dict(extra, experts_touched=n_act))
+
+    xs_host = [S.bf16_tensor_to_bits(x) for x in xs[:2]]
+    e2e = e2e_run(args, fwd, xs_host, (T_r, H), dev, timer)
     cpu = None
     if rank == 0 and world == 1:
-        cpu = cpu_baseline(bw_host, xs_host[0][: min(T, 128)], args.cpu_seconds)
-        if T > 128:
-            cpu["sample"] += f" ({min(T, 128)} of the {T} tokens; rows are independent)"
+        bw0 = S.host_block(cfg, 1)
+        cpu = cpu_baseline(bw0, S.host_x(5, 128, H), min(args.cpu_seconds, 8.0))
+        cpu["value"] /= layers
+        cpu["sample"] += f" of one block, rate divided by the {layers} blocks"
+    P_all = T * cfg.top_k
     if world > 1:
-        torch.cuda.synchronize()
-        dist.barrier()
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"{cfg.name} MoE block {regime}, T={T} tokens per GPU", "global_batch": T * world,
-                       "seq_len": 1, "parallelism": f"replicas{world}" if world > 1 else "single",
-                       "experts": cfg.num_experts, "top_k": cfg.top_k, "hidden": H, "moe_inter": cfg.moe_inter,
-                       "l2": "flushed (256 MiB write) before every timed step", "launch": mode,
-                       "clock_window": "nvidia-smi every 200 ms across 0.6 s of untimed steps, the timed steps, 0.6 s more",
-                       "distinct_experts_per_step": U, "sweep_eager": sweep},
-            "roofline": roof,
-            "cpu_baseline": cpu,
-            "e2e": {"value": world * T / (e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
-                    "d2h_bytes_per_step": T * H * 2, "ms_per_step": e2e},
-            "gpu_launches": LAUNCHES_PER_STEP * args.steps,
-            "clocks": clock_info,
-            "library": mlx_rs_b200.library_path,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        del graph
-        dist.destroy_process_group()
+        per_block = 4 + 2 + group_launches(P_all, n)
+    else:
+        per_block = 5 + group_launches(P_all, cfg.num_experts) + 1  # + RMSNorm
+    return {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{cfg.name} stack of {layers} MoE blocks + RMSNorm, {regime}, T={T} tokens in total",
+                   "global_batch": T, "tokens_per_gpu": T_r, "seq_len": 1,
+                   "parallelism": f"ep{world}" if world > 1 else "single", "experts_per_gpu": n,
+                   "l2": "inputs larger than L2 (each step streams every block's weights)", "launch": mode,
+                   "clock_window": "nvidia-smi every 200 ms across 0.6 s of untimed steps, the timed steps, 0.6 s more"},
+        "roofline": roof,
+        "cpu_baseline": cpu,
+        "e2e": {"value": T / (e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T_r * H * 2,
+                "d2h_bytes_per_step": T_r * H * 2, "ms_per_step": e2e},
+        "gpu_launches": per_block * layers * args.steps,
+        "clocks": clock_info,
+        "library": mlx_rs_b200.library_path,
+    }
 
 
 if __name__ == "__main__":

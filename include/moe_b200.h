@@ -185,6 +185,58 @@ int moe_block_profile(moe_ctx* ctx, const moe_block_config* cfg, const moe_block
                       const void* x, int64_t T, void* out, float* stage_ms, int32_t* n_active);
 
 /*
+ * Status word of the context's device work: nonzero after a bounded device-side wait
+ * expired in a kernel launched on this context (the kernel then stopped early and its
+ * outputs are invalid). Synchronises the context's stream. No counterpart in the
+ * reference (MLX kernels do not wait on barriers with a time limit).
+ */
+int moe_ctx_status(moe_ctx* ctx, int32_t* status);
+
+/*
+ * Expert parallelism (EP) over `world` ranks, one process and one context per GPU.
+ * Rank r holds the router, expert_bias and the experts [expert_begin, expert_begin +
+ * num_local) of every block, and its own T_r tokens. One block on every rank is:
+ *   1. moe_ep_route(x_r)                       -> packed_r [T_r, k]
+ *   2. all-gather x_r -> x_all [T_all, H] and packed_r -> packed_all [T_all, k]
+ *      (every rank's tokens in rank order; NCCL, by the host)
+ *   3. moe_ep_experts(x_all, packed_all)       -> partial [T_all, H] fp32
+ *   4. all-to-all of partial in equal parts of T_r rows: rank s sends rows
+ *      [r*T_r, (r+1)*T_r) of its partial to rank r (NCCL, by the host)
+ *   5. moe_ep_finish(received [world, T_r, H]) -> out_r [T_r, H] (+ next RMSNorm)
+ * The block's routing is that of moe_block_forward, bit for bit; the output differs
+ * from it only in the fp32 association of the k-term sum (ranks' partial sums are
+ * added in rank order), i.e. by last-bit rounding. These replace
+ * SparseMoeBlock::forward (qwen3_moe_python_port.rs:420-488) when its experts are
+ * sharded; the reference runs on one device and has no EP, so the split itself has
+ * no reference counterpart. Blocks with a shared expert are not supported here
+ * (MOE_ERR_UNSUPPORTED).
+ */
+
+/* Routing of this rank's tokens: packed[T, k] = expert | bf16(weight) << 16, the
+ * experts and weights of moe_block_route (qwen3_moe_python_port.rs:436-445,
+ * lfm2_moe_python_port.rs:559-586). Reads only wts->router and wts->expert_bias. */
+int moe_ep_route(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts,
+                 const void* x, int64_t T, uint32_t* packed);
+
+/* This rank's experts over every rank's tokens: partial[t, :] (fp32) = sum over
+ * j = 0..k-1 in order, of the pairs (t, j) whose expert lies in [expert_begin,
+ * expert_begin + num_local), of bf16(expert_out * weight) (the weighted combine of
+ * qwen3_moe_python_port.rs:471-472 restricted to these experts, not rounded); zero
+ * rows for tokens that chose none of them. cfg->num_experts is the global E; the
+ * gate/up/down tensors of wts hold the num_local local experts, [num_local, N, K/8].
+ * Scratch covers the worst case of every pair being local (T_all*k rows). */
+int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts,
+                   const void* x_all, int64_t T_all, const uint32_t* packed_all,
+                   int32_t expert_begin, int32_t num_local, float* partial);
+
+/* out[r] = bf16(sum over s = 0..world-1 in order of partials[s, r, :]) for r < rows
+ * (partials [world, rows, hidden] fp32, the all-to-all's output). With norm_weight
+ * (and normed), also normed[r] = moe_fast_rms_norm(out[r], norm_weight, eps): the
+ * RMSNorm before the next block of a stack, fused. */
+int moe_ep_finish(moe_ctx* ctx, const float* partials, int32_t world, int64_t rows,
+                  int64_t hidden, void* out, const void* norm_weight, float eps, void* normed);
+
+/*
  * moe_gather_qmm without any device allocation. Same arguments, semantics and results
  * as moe_gather_qmm; no counterpart in the reference (mlx-c allocates through MLX's own
  * allocator). For callers that cannot let a library allocate GPU memory: a host

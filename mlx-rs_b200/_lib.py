@@ -86,6 +86,14 @@ SIGNATURES = {
     "moe_block_route": (C.c_int, [C.c_void_p, C.POINTER(BlockConfig), C.POINTER(BlockWeights),
                                   C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p,
                                   C.c_void_p]),
+    "moe_ctx_status": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
+    "moe_ep_route": (C.c_int, [C.c_void_p, C.POINTER(BlockConfig), C.POINTER(BlockWeights),
+                               C.c_void_p, C.c_int64, C.c_void_p]),
+    "moe_ep_experts": (C.c_int, [C.c_void_p, C.POINTER(BlockConfig), C.POINTER(BlockWeights),
+                                 C.c_void_p, C.c_int64, C.c_void_p, C.c_int32, C.c_int32,
+                                 C.c_void_p]),
+    "moe_ep_finish": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int64, C.c_int64,
+                                C.c_void_p, C.c_void_p, C.c_float, C.c_void_p]),
 }
 
 

@@ -193,6 +193,93 @@ int check_block(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights
   return MOE_OK;
 }
 
+// Router-side checks only (the expert-parallel route needs no expert weights).
+int check_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* w, const char* fn) {
+  if (!c) return fail(ctx, MOE_ERR_INVALID, "%s: null config", fn);
+  int rc = check_quant(ctx, fn, c->hidden, c->group_size, c->bits);
+  if (rc) return rc;
+  if (c->num_experts <= 0 || c->num_experts > 512)
+    return fail(ctx, MOE_ERR_UNSUPPORTED, "%s: num_experts=%d (supported 1..512)", fn, c->num_experts);
+  if (c->top_k <= 0 || c->top_k > 32 || c->top_k > c->num_experts)
+    return fail(ctx, MOE_ERR_INVALID, "%s: top_k=%d (1..min(32, num_experts))", fn, c->top_k);
+  if (c->scoring < 0 || c->scoring > 2) return fail(ctx, MOE_ERR_INVALID, "%s: scoring=%d", fn, c->scoring);
+  if (c->shared_inter != 0)
+    return fail(ctx, MOE_ERR_UNSUPPORTED, "%s: the expert-parallel path has no shared expert (shared_inter=%d)", fn,
+                c->shared_inter);
+  if (!w || !w->router.w || !w->router.scales) return fail(ctx, MOE_ERR_INVALID, "%s: router weight missing", fn);
+  if (c->scoring != MOE_SCORING_SOFTMAX && !w->expert_bias)
+    return fail(ctx, MOE_ERR_INVALID, "%s: scoring mode %d needs expert_bias", fn, c->scoring);
+  if (!aligned16(w->router.w)) return fail(ctx, MOE_ERR_INVALID, "%s: weight pointers must be 16-byte aligned", fn);
+  return MOE_OK;
+}
+
+// Expert-side checks of the expert-parallel experts call (the router is not read).
+int check_experts(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* w, const char* fn) {
+  if (!c) return fail(ctx, MOE_ERR_INVALID, "%s: null config", fn);
+  int rc = check_quant(ctx, fn, c->hidden, c->group_size, c->bits);
+  if (rc) return rc;
+  if (c->num_experts <= 0 || c->num_experts > 512)
+    return fail(ctx, MOE_ERR_UNSUPPORTED, "%s: num_experts=%d (supported 1..512)", fn, c->num_experts);
+  if (c->top_k <= 0 || c->top_k > 32 || c->top_k > c->num_experts)
+    return fail(ctx, MOE_ERR_INVALID, "%s: top_k=%d (1..min(32, num_experts))", fn, c->top_k);
+  if (c->moe_inter <= 0 || c->moe_inter % 64 != 0)
+    return fail(ctx, MOE_ERR_INVALID, "%s: moe_inter=%d must be a positive multiple of 64", fn, c->moe_inter);
+  if (c->shared_inter != 0)
+    return fail(ctx, MOE_ERR_UNSUPPORTED, "%s: the expert-parallel path has no shared expert (shared_inter=%d)", fn,
+                c->shared_inter);
+  if (!w) return fail(ctx, MOE_ERR_INVALID, "%s: null weights", fn);
+  const moe_qweight* need[3] = {&w->gate, &w->up, &w->down};
+  for (const moe_qweight* q : need) {
+    if (!q->w || !q->scales) return fail(ctx, MOE_ERR_INVALID, "%s: expert weights missing", fn);
+    if (!aligned16(q->w)) return fail(ctx, MOE_ERR_INVALID, "%s: weight pointers must be 16-byte aligned", fn);
+  }
+  return MOE_OK;
+}
+
+// Routing workspace of T tokens: the status word, the logits and the top-k scratch.
+BlockWs carve_route(void* base, const moe_block_config* c, int64_t T) {
+  Carve cv(base);
+  BlockWs w{};
+  const int64_t E = c->num_experts, P = T * c->top_k;
+  w.status = cv.take<int32_t>(64);
+  w.logits = cv.take<uint16_t>(T * (E + 1));
+  w.idx = cv.take<uint32_t>(P);
+  w.wsel = cv.take<uint16_t>(P);
+  w.gate_val = cv.take<uint16_t>(T);
+  w.bytes = cv.off + 256;
+  return w;
+}
+
+// Workspace of an expert-parallel experts call over T tokens (every rank's tokens)
+// with El local experts; sized for the worst case of every pair being local.
+struct EpWs {
+  int32_t* status;
+  int32_t *hist, *segbase, *offsets, *active, *n_active, *tile_start;
+  uint32_t *perm, *inv;
+  uint16_t *hbuf, *ybuf;
+  size_t bytes;
+};
+
+EpWs carve_ep(void* base, const moe_block_config* c, int64_t T, int El) {
+  Carve cv(base);
+  EpWs w{};
+  const int64_t P = T * c->top_k;
+  const int64_t nseg = std::max<int64_t>(1, (P + kGroupSeg - 1) / kGroupSeg);
+  w.status = cv.take<int32_t>(64);  // first, at the fixed offset every workspace shares
+  w.hist = cv.take<int32_t>(nseg * El);
+  w.segbase = cv.take<int32_t>(nseg * El);
+  w.offsets = cv.take<int32_t>(El + 1);
+  w.active = cv.take<int32_t>(El);
+  w.n_active = cv.take<int32_t>(1);
+  w.tile_start = cv.take<int32_t>(El + 1);
+  w.perm = cv.take<uint32_t>(P);
+  w.inv = cv.take<uint32_t>(P);
+  w.hbuf = cv.take<uint16_t>(P * c->moe_inter);
+  w.ybuf = cv.take<uint16_t>(P * c->hidden);
+  w.bytes = cv.off + 256;
+  return w;
+}
+
 // Stage boundaries recorded by moe_block_profile (ev == null: not recorded).
 enum Stage { kRouter = 0, kTopk, kGroup, kGateUp, kDown, kSharedGateUp, kSharedDown, kCombine, kStages };
 
@@ -202,8 +289,10 @@ enum Stage { kRouter = 0, kTopk, kGroup, kGateUp, kDown, kSharedGateUp, kSharedD
   } while (0)
 
 // Routing + grouping of one block call into ws.
+// With `packed`, routing writes [T, k] expert | bf16(weight) << 16 there and stops
+// before the grouping (the expert-parallel route).
 int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* w, const void* x, int64_t T,
-              const BlockWs& ws, cudaEvent_t* ev = nullptr) {
+              const BlockWs& ws, cudaEvent_t* ev = nullptr, uint32_t* packed = nullptr) {
   const int E = c->num_experts;
   const bool gate_row = c->shared_inter > 0 && c->has_shared_gate;
   moe::RouterArgs ra{};
@@ -232,11 +321,13 @@ int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* 
   ta.scoring = c->scoring;
   ta.norm_topk_prob = c->norm_topk_prob;
   ta.expert_bias = static_cast<const uint16_t*>(w->expert_bias);
-  ta.idx = ws.idx;
-  ta.weights = ws.wsel;
+  ta.idx = packed ? nullptr : ws.idx;
+  ta.weights = packed ? nullptr : ws.wsel;
+  ta.packed = packed;
   ta.gate_val = gate_row ? ws.gate_val : nullptr;
   MOE_MARK(ev, kTopk, ctx->stream);
   MOE_CUDA(ctx, moe::launch_topk(ta, ctx->stream));
+  if (packed) return MOE_OK;
 
   moe::GroupArgs ga{};
   ga.key = ws.idx;
@@ -610,6 +701,150 @@ int moe_block_profile(moe_ctx* ctx, const moe_block_config* cfg, const moe_block
   }
   for (int i = 0; i <= kStages; ++i) cudaEventDestroy(ev[i]);
   return rc;
+}
+
+// ---------------------------------------------------------------------------------
+// Expert parallelism
+// ---------------------------------------------------------------------------------
+
+int moe_ep_route(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x,
+                 int64_t T, uint32_t* packed) {
+  if (!ctx) return MOE_ERR_INVALID;
+  ctx->last_error.clear();
+  const char* fn = "moe_ep_route";
+  int rc = check_route(ctx, cfg, wts, fn);
+  if (rc) return rc;
+  if (T < 0 || T > (INT32_MAX / 64)) return fail(ctx, MOE_ERR_INVALID, "%s: bad T", fn);
+  if (T == 0) return MOE_OK;
+  if (!x || !packed || !aligned16(x)) return fail(ctx, MOE_ERR_INVALID, "%s: x must be 16-byte aligned, packed non-null", fn);
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  rc = ensure_scratch(ctx, carve_route(nullptr, cfg, T).bytes);
+  if (rc) return rc;
+  return run_route(ctx, cfg, wts, x, T, carve_route(ctx->scratch, cfg, T), nullptr, packed);
+}
+
+int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x_all,
+                   int64_t T_all, const uint32_t* packed_all, int32_t expert_begin, int32_t num_local,
+                   float* partial) {
+  if (!ctx) return MOE_ERR_INVALID;
+  ctx->last_error.clear();
+  const char* fn = "moe_ep_experts";
+  int rc = check_experts(ctx, cfg, wts, fn);
+  if (rc) return rc;
+  if (num_local <= 0 || expert_begin < 0 || (int64_t)expert_begin + num_local > cfg->num_experts)
+    return fail(ctx, MOE_ERR_INVALID, "%s: experts [%d, %d + %d) outside [0, %d)", fn, expert_begin, expert_begin,
+                num_local, cfg->num_experts);
+  if (T_all < 0 || T_all > (INT32_MAX / 64)) return fail(ctx, MOE_ERR_INVALID, "%s: bad T_all", fn);
+  if (T_all == 0) return MOE_OK;
+  if (!x_all || !packed_all || !partial || !aligned16(x_all) || !aligned16(partial))
+    return fail(ctx, MOE_ERR_INVALID, "%s: x_all and partial must be non-null and 16-byte aligned", fn);
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  rc = ensure_scratch(ctx, carve_ep(nullptr, cfg, T_all, num_local).bytes);
+  if (rc) return rc;
+  const EpWs ws = carve_ep(ctx->scratch, cfg, T_all, num_local);
+  const int E = cfg->num_experts, El = num_local, H = cfg->hidden, I = cfg->moe_inter, k = cfg->top_k;
+  const int64_t P = T_all * k;
+
+  moe::GroupArgs ga{};
+  ga.key = packed_all;
+  ga.key_packed = 1;
+  ga.key_base = (uint32_t)expert_begin;
+  ga.P = P;
+  ga.E = El;
+  ga.seg = kGroupSeg;
+  ga.nseg = (int)std::max<int64_t>(1, (P + kGroupSeg - 1) / kGroupSeg);
+  ga.hist = ws.hist;
+  ga.segbase = ws.segbase;
+  ga.offsets = ws.offsets;
+  ga.active = ws.active;
+  ga.n_active = ws.n_active;
+  ga.perm = ws.perm;
+  ga.inv = ws.inv;
+  ga.tile_start = ws.tile_start;
+  ga.tile_rows = moe::kTcTileRows;
+  MOE_CUDA(ctx, moe::launch_group(ga, ctx->stream));
+
+  // Path choice on the expected rows per expert (all pairs over all E experts); the
+  // grids cover every local pair in the worst case and idle CTAs leave at once.
+  const bool tc_gu = use_tc(P, E, I, H), tc_dn = use_tc(P, E, H, I);
+  const int slots = (int)std::min<int64_t>(P, El);
+  const int max_tiles = (int)(P / moe::kTcTileRows + std::min<int64_t>(El, P) + 1);
+  moe::QgemvArgs gu = qgemv_args(wts->gate, &wts->up, I, H);
+  gu.x = static_cast<const uint16_t*>(x_all);
+  gu.x_mode = 1;
+  gu.x_repeat = k;
+  gu.perm = ws.perm;
+  gu.offsets = ws.offsets;
+  gu.active = ws.active;
+  gu.n_active = ws.n_active;
+  gu.out = ws.hbuf;
+  if (tc_gu) {
+    moe::TcGemmArgs ta{gu, ws.tile_start, El, max_tiles, ws.status};
+    MOE_CUDA(ctx, moe::launch_tc_gemm(ta, true, ctx->stream));
+  } else {
+    MOE_CUDA(ctx, moe::launch_qgemv(gu, true, slots, 8, ctx->stream));
+  }
+  moe::QgemvArgs dn = qgemv_args(wts->down, nullptr, H, I);
+  dn.x = ws.hbuf;
+  dn.x_mode = 0;
+  dn.perm = ws.perm;
+  dn.offsets = ws.offsets;
+  dn.active = ws.active;
+  dn.n_active = ws.n_active;
+  dn.out = ws.ybuf;
+  if (tc_dn) {
+    moe::TcGemmArgs ta{dn, ws.tile_start, El, max_tiles, ws.status};
+    MOE_CUDA(ctx, moe::launch_tc_gemm(ta, false, ctx->stream));
+  } else {
+    MOE_CUDA(ctx, moe::launch_qgemv(dn, false, slots, 8, ctx->stream));
+  }
+  moe::EpPartialArgs pa{};
+  pa.y = ws.ybuf;
+  pa.inv = ws.inv;
+  pa.packed = packed_all;
+  pa.e0 = (uint32_t)expert_begin;
+  pa.E_l = El;
+  pa.T = (int)T_all;
+  pa.k = k;
+  pa.H = H;
+  pa.partial = partial;
+  MOE_CUDA(ctx, moe::launch_ep_partial(pa, ctx->stream));
+  return MOE_OK;
+}
+
+int moe_ep_finish(moe_ctx* ctx, const float* partials, int32_t world, int64_t rows, int64_t hidden, void* out,
+                  const void* norm_weight, float eps, void* normed) {
+  if (!ctx) return MOE_ERR_INVALID;
+  ctx->last_error.clear();
+  const char* fn = "moe_ep_finish";
+  if (world <= 0 || rows < 0 || hidden <= 0 || hidden % 8 != 0 || hidden > INT32_MAX)
+    return fail(ctx, MOE_ERR_INVALID, "%s: bad world/rows/hidden (hidden a positive multiple of 8)", fn);
+  if (rows == 0) return MOE_OK;
+  if (!partials || !out || !aligned16(partials) || !aligned16(out))
+    return fail(ctx, MOE_ERR_INVALID, "%s: partials and out must be non-null and 16-byte aligned", fn);
+  if ((norm_weight == nullptr) != (normed == nullptr))
+    return fail(ctx, MOE_ERR_INVALID, "%s: norm_weight and normed go together", fn);
+  if (norm_weight && (!aligned16(norm_weight) || !aligned16(normed)))
+    return fail(ctx, MOE_ERR_INVALID, "%s: norm_weight and normed must be 16-byte aligned", fn);
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  MOE_CUDA(ctx, moe::launch_ep_finish(partials, world, rows, (int)hidden, static_cast<uint16_t*>(out),
+                                      static_cast<const uint16_t*>(norm_weight), eps,
+                                      static_cast<uint16_t*>(normed), ctx->stream));
+  return MOE_OK;
+}
+
+int moe_ctx_status(moe_ctx* ctx, int32_t* status) {
+  if (!ctx || !status) return MOE_ERR_INVALID;
+  *status = 0;
+  if (!ctx->scratch) return MOE_OK;
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  MOE_CUDA(ctx, cudaMemcpyAsync(status, ctx->scratch, sizeof(int32_t), cudaMemcpyDeviceToHost, ctx->stream));
+  MOE_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  return MOE_OK;
 }
 
 }  // extern "C"

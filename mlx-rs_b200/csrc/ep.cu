@@ -1,0 +1,128 @@
+// ep.cu — the two kernels that expert parallelism adds around the block's kernels.
+//
+// Under expert parallelism rank r owns experts [e0, e0 + E_l) of every block and the
+// tokens [r*T_l, (r+1)*T_l). Each rank routes its own tokens, the token rows and their
+// packed routing (expert | bf16 weight << 16) are all-gathered, every rank runs its
+// experts over the pairs that selected them, and the per-token partial sums travel back
+// to the token's owner with an all-to-all, where they are added in rank order.
+//
+// ep_partial: the combine of SparseMoeBlock::forward (expert_out * score, sum_axis(1),
+//   qwen3_moe_python_port.rs:471-472; lfm2_moe_python_port.rs:718-732) restricted to
+//   the local experts: partial[t] = sum over j = 0..k-1 in index order, of the local
+//   pairs only, of bf16(y * w_j), in fp32 and not rounded (the owner rounds once).
+//   Each thread owns 8 consecutive hidden elements of one token, as in combine.cu.
+// ep_finish: out[t] = bf16(sum over ranks s in order of partial_s[t]); optionally the
+//   next block's RMSNorm (RmsNorm::forward, crates/mlx-nn/src/rms_norm.rs:30-34) of
+//   out in the same pass, with the canonical sum of squares of rms_norm_kernel.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace moe {
+
+__global__ void __launch_bounds__(256) ep_partial_kernel(EpPartialArgs a) {
+  const int vec_per_row = a.H >> 3;
+  const int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  if (id >= (int64_t)a.T * vec_per_row) return;
+  const int t = (int)(id / vec_per_row);
+  const int h = (int)(id - (int64_t)t * vec_per_row) * 8;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+  for (int j = 0; j < a.k; ++j) {
+    const int64_t p = (int64_t)t * a.k + j;
+    const uint32_t pk = a.packed[p];
+    if ((pk & 0xffffu) - a.e0 >= (uint32_t)a.E_l) continue;  // another rank's expert
+    const float wj = bf2f((uint16_t)(pk >> 16));
+    const uint4 v = *reinterpret_cast<const uint4*>(a.y + (size_t)a.inv[p] * a.H + h);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      acc[2 * i] = __fadd_rn(acc[2 * i], rbf(__fmul_rn(bf_lo(u[i]), wj)));
+      acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], rbf(__fmul_rn(bf_hi(u[i]), wj)));
+    }
+  }
+  float4* dst = reinterpret_cast<float4*>(a.partial + (size_t)t * a.H + h);
+  dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+}
+
+// One warp per row; lane l owns the chunks of 8 elements c = l, l + 32, ...
+__global__ void __launch_bounds__(256) ep_finish_kernel(const float* __restrict__ recv, int world, int64_t rows,
+                                                        int H, uint16_t* __restrict__ out,
+                                                        const uint16_t* __restrict__ norm_w, float eps,
+                                                        uint16_t* __restrict__ normed) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  pdl_wait();
+  pdl_trigger();
+  if (r >= rows) return;
+  const int nchunks = H >> 3;
+  const size_t rank_stride = (size_t)rows * H;
+  float ss = 0.0f;
+  for (int c = lane; c < nchunks; c += 32) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    for (int s = 0; s < world; ++s) {
+      const float4* src = reinterpret_cast<const float4*>(recv + s * rank_stride + (size_t)r * H + c * 8);
+      const float4 x0 = src[0], x1 = src[1];
+      v[0] = __fadd_rn(v[0], x0.x);
+      v[1] = __fadd_rn(v[1], x0.y);
+      v[2] = __fadd_rn(v[2], x0.z);
+      v[3] = __fadd_rn(v[3], x0.w);
+      v[4] = __fadd_rn(v[4], x1.x);
+      v[5] = __fadd_rn(v[5], x1.y);
+      v[6] = __fadd_rn(v[6], x1.z);
+      v[7] = __fadd_rn(v[7], x1.w);
+    }
+    uint16_t o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      o[i] = f2bf(v[i]);
+      const float q = bf2f(o[i]);
+      ss = __fmaf_rn(q, q, ss);
+    }
+    uint4 ov;
+    ov.x = (uint32_t)o[0] | ((uint32_t)o[1] << 16);
+    ov.y = (uint32_t)o[2] | ((uint32_t)o[3] << 16);
+    ov.z = (uint32_t)o[4] | ((uint32_t)o[5] << 16);
+    ov.w = (uint32_t)o[6] | ((uint32_t)o[7] << 16);
+    *reinterpret_cast<uint4*>(out + (size_t)r * H + c * 8) = ov;
+  }
+  if (!norm_w) return;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+  const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), eps)));
+  for (int c = lane; c < nchunks; c += 32) {
+    // this thread's own stores above
+    const uint4 v = *reinterpret_cast<const uint4*>(out + (size_t)r * H + c * 8);
+    const uint4 wv = *reinterpret_cast<const uint4*>(norm_w + c * 8);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint16_t lo = f2bf(__fmul_rn(rbf(__fmul_rn(bf_lo(u[i]), rr)), bf_lo(wu[i])));
+      const uint16_t hi = f2bf(__fmul_rn(rbf(__fmul_rn(bf_hi(u[i]), rr)), bf_hi(wu[i])));
+      o[i] = (uint32_t)lo | ((uint32_t)hi << 16);
+    }
+    *reinterpret_cast<uint4*>(normed + (size_t)r * H + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+cudaError_t launch_ep_partial(const EpPartialArgs& a, cudaStream_t st) {
+  const int64_t n = (int64_t)a.T * (a.H >> 3);
+  if (n <= 0) return cudaSuccess;
+  return launch_k(ep_partial_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, a);
+}
+
+cudaError_t launch_ep_finish(const float* recv, int world, int64_t rows, int H, uint16_t* out,
+                             const uint16_t* norm_w, float eps, uint16_t* normed, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  return launch_k(ep_finish_kernel, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0, st, recv, world, rows, H, out,
+                  norm_w, eps, normed);
+}
+
+}  // namespace moe

@@ -21,6 +21,12 @@
 
 namespace moe {
 
+MOE_DEV uint32_t group_key(const GroupArgs& a, int64_t p) {
+  uint32_t v = a.key[p];
+  if (a.key_packed) v &= 0xffffu;
+  return v - a.key_base;
+}
+
 // Block-wide exclusive scan of one value per thread (thread order); returns the
 // exclusive prefix and writes the total to *total (1024 threads).
 MOE_DEV int32_t block_exclusive_scan(int32_t v, int32_t* warp_tot, int32_t* total) {
@@ -63,7 +69,7 @@ __global__ void __launch_bounds__(1024) group_small_kernel(GroupArgs a) {
   const int64_t p0 = warp * seg;
   const int64_t p1 = (p0 + seg < a.P) ? p0 + seg : a.P;
   for (int64_t p = p0 + lane; p < p1; p += 32) {
-    const uint32_t e = a.key[p];
+    const uint32_t e = group_key(a, p);
     if (e < (uint32_t)E) atomicAdd(&wbase[warp * E + e], 1);
   }
   __syncthreads();
@@ -97,7 +103,7 @@ __global__ void __launch_bounds__(1024) group_small_kernel(GroupArgs a) {
   for (int64_t b = p0; b < p1; b += 32) {
     const int64_t p = b + lane;
     const bool valid = p < p1;
-    const uint32_t e = valid ? a.key[p] : 0xffffffffu;
+    const uint32_t e = valid ? group_key(a, p) : 0xffffffffu;
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const unsigned lt = (1u << lane) - 1u;
     int32_t pos = 0;
@@ -121,7 +127,7 @@ __global__ void group_hist_kernel(GroupArgs a) {
   const int64_t p0 = (int64_t)g * a.seg;
   const int64_t p1 = (p0 + a.seg < a.P) ? p0 + a.seg : a.P;
   for (int64_t p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
-    const uint32_t e = a.key[p];
+    const uint32_t e = group_key(a, p);
     if (e < (uint32_t)a.E) atomicAdd(&sh[e], 1);
   }
   __syncthreads();
@@ -223,7 +229,7 @@ __global__ void group_scatter_kernel(GroupArgs a) {
   for (int64_t base = p0; base < p1; base += 32) {
     const int64_t p = base + lane;
     const bool valid = p < p1;
-    const uint32_t e = valid ? a.key[p] : 0xffffffffu;
+    const uint32_t e = valid ? group_key(a, p) : 0xffffffffu;
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const unsigned lt = (1u << lane) - 1u;
     int32_t pos = 0;

@@ -50,11 +50,16 @@ struct TopkArgs {
   uint32_t* idx;                // [T, k]
   uint16_t* weights;            // [T, k] bf16
   uint16_t* gate_val;           // [T] bf16 = sigmoid(logits[:, E]) or null
+  uint32_t* packed;             // [T, k] idx | bf16(weight) << 16, or null
 };
 
-// Stable grouping of P pair ids by expert id (key[p] < E).
+// Stable grouping of P pair ids by expert id. The expert of pair p is
+// (key_packed ? key[p] & 0xffff : key[p]) - key_base; pairs whose expert falls
+// outside [0, E) are left out (offsets[E] counts the pairs kept).
 struct GroupArgs {
   const uint32_t* key;  // [P]
+  int key_packed;
+  uint32_t key_base;
   int64_t P;
   int E;
   int seg;          // pairs per segment
@@ -124,6 +129,23 @@ constexpr int kTcTileRows = 256;
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, bool gated, cudaStream_t st);
 
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st);
+
+// Expert parallelism. Partial combine of one rank's experts [e0, e0 + E_l):
+// partial[t, :] (fp32) = sum over j = 0..k-1 in order, of the pairs p = t*k + j whose
+// expert is local, of bf16(y[inv[p], :] * weight_p); zero for tokens with none.
+struct EpPartialArgs {
+  const uint16_t* y;        // [local pairs, H] expert outputs in grouped order
+  const uint32_t* inv;      // [T*k] pair -> grouped row (written for local pairs only)
+  const uint32_t* packed;   // [T, k] expert | bf16(weight) << 16
+  uint32_t e0;
+  int E_l, T, k, H;
+  float* partial;           // [T, H]
+};
+cudaError_t launch_ep_partial(const EpPartialArgs& a, cudaStream_t st);
+// out[r] = bf16(sum over ranks s = 0..world-1 in order of recv[s, r, :]) for r < rows;
+// with norm_w, also normed[r] = RMSNorm(out[r]) * norm_w as launch_rms_norm computes it.
+cudaError_t launch_ep_finish(const float* recv, int world, int64_t rows, int H, uint16_t* out,
+                             const uint16_t* norm_w, float eps, uint16_t* normed, cudaStream_t st);
 cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, float eps, int64_t rows, int dim,
                             uint16_t* out, cudaStream_t st);
 

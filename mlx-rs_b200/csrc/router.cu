@@ -229,8 +229,10 @@ __global__ void __launch_bounds__(128) topk_kernel(TopkArgs a) {
     my_w = rbf(__fdiv_rn(my_w, d));
   }
   if (lane < a.k) {
-    a.idx[(size_t)t * a.k + lane] = (uint32_t)my_sel;
-    a.weights[(size_t)t * a.k + lane] = f2bf(my_w);
+    const uint16_t wb = f2bf(my_w);
+    if (a.idx) a.idx[(size_t)t * a.k + lane] = (uint32_t)my_sel;
+    if (a.weights) a.weights[(size_t)t * a.k + lane] = wb;
+    if (a.packed) a.packed[(size_t)t * a.k + lane] = (uint32_t)my_sel | ((uint32_t)wb << 16);
   }
   if (a.gate_val && lane == 0) a.gate_val[t] = f2bf(sigmoid_canon(bf2f(lrow[a.E])));
 }

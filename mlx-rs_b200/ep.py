@@ -1,0 +1,182 @@
+"""Expert parallelism (EP) of the MoE block over torch.distributed ranks, one GPU each.
+
+The reference runs a block on one device (SparseMoeBlock::forward,
+qwen3_moe_python_port.rs:420-488). Its experts shard naturally: rank r of `world`
+holds the router (replicated) and experts [r*E/world, (r+1)*E/world) of every block,
+and owns T_r tokens of the batch (the same T_r on every rank). One block is
+
+    packed_r  = route(x_r)                          moe_ep_route      [T_r, k] u32
+    x_all     = all_gather(x_r)                     NCCL              [world*T_r, H]
+    pk_all    = all_gather(packed_r)                NCCL              [world*T_r, k]
+    partial   = experts(x_all, pk_all)              moe_ep_experts    [world*T_r, H] fp32
+    received  = all_to_all(partial)                 NCCL, equal parts [world, T_r, H] fp32
+    out_r     = finish(received) (+ next RMSNorm)   moe_ep_finish     [T_r, H] bf16
+
+Dispatch is an all-gather rather than a variable all-to-all: with top-8 of 128 experts
+a token reaches 5.3 of 8 ranks on average (1.6 of 2 at world 2), so the gather moves at
+most 1.6x the rows a deduplicated all-to-all would, and it needs no per-step counts on
+the host. Nothing in a block waits for the host, so a whole stack of blocks, the
+collectives included, can be captured in one CUDA graph. The combine all-to-all returns
+fp32 partial sums, which the owner adds in rank order; routing is bit-identical to the
+single-device block, outputs differ only by the fp32 association of the k-term sum.
+
+The compute steps are supplied by an `ops` object so that the same orchestration runs
+on the CUDA library (CudaEpOps, the default and the only product implementation) or,
+in tests, on any other implementation of the three steps with the gloo backend.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import replace
+from typing import Optional, Sequence
+
+import torch
+import torch.distributed as dist
+
+from ._lib import MlxError, library
+from .block import _Block
+from .ops import _ctx, _ptr
+from .synth import BlockWeights, MoeConfig, QWeight
+
+
+def expert_range(num_experts: int, world: int, rank: int):
+    """(expert_begin, num_local) of `rank`: equal contiguous shares of the experts."""
+    if world <= 0 or not 0 <= rank < world:
+        raise MlxError("expert_range", 1, f"rank {rank} of world {world}")
+    if num_experts % world:
+        raise MlxError("expert_range", 1, f"{num_experts} experts do not split evenly over {world} ranks")
+    n = num_experts // world
+    return rank * n, n
+
+
+def local_weights(full: BlockWeights, expert_begin: int, num_local: int) -> BlockWeights:
+    """The rank's share of a block: router and expert_bias whole, experts sliced."""
+    def sl(q: QWeight) -> QWeight:
+        e0, e1 = expert_begin, expert_begin + num_local
+        return QWeight(q.w[e0:e1].contiguous(), q.scales[e0:e1].contiguous(),
+                       None if q.biases is None else q.biases[e0:e1].contiguous())
+    if full.config.shared_inter:
+        raise MlxError("moe_ep_experts", 2, "the expert-parallel path has no shared expert")
+    return BlockWeights(full.config, full.router, sl(full.gate), sl(full.up), sl(full.down), full.expert_bias)
+
+
+class CudaEpOps:
+    """The three EP compute steps on libmoe_b200.so (moe_ep_route / _experts / _finish)."""
+
+    def bind(self, weights: BlockWeights, config: MoeConfig):
+        return _Block(weights, config)
+
+    def route(self, blk: _Block, x: torch.Tensor, packed: torch.Tensor):
+        ctx = _ctx(x)
+        T = x.shape[0]
+        ctx.check("moe_ep_route", library().moe_ep_route(ctx.handle, C.byref(blk._cfg), C.byref(blk._wts),
+                                                          _ptr(x), T, _ptr(packed)))
+
+    def experts(self, blk: _Block, x_all, packed_all, expert_begin: int, num_local: int, partial):
+        ctx = _ctx(x_all)
+        ctx.check("moe_ep_experts", library().moe_ep_experts(
+            ctx.handle, C.byref(blk._cfg), C.byref(blk._wts), _ptr(x_all), x_all.shape[0], _ptr(packed_all),
+            expert_begin, num_local, _ptr(partial)))
+
+    def finish(self, received, world: int, out, norm_weight=None, eps: float = 1e-6, normed=None):
+        ctx = _ctx(received)
+        rows, H = out.shape
+        ctx.check("moe_ep_finish", library().moe_ep_finish(ctx.handle, _ptr(received), world, rows, H, _ptr(out),
+                                                            _ptr(norm_weight), C.c_float(eps), _ptr(normed)))
+
+
+class _Buffers:
+    """Per-(tokens per rank) exchange buffers, reused by every block of a stack."""
+
+    def __init__(self, T: int, H: int, k: int, world: int, device):
+        self.T = T
+        self.packed = torch.empty(T, k, dtype=torch.int32, device=device)
+        self.x_all = torch.empty(world * T, H, dtype=torch.bfloat16, device=device)
+        self.packed_all = torch.empty(world * T, k, dtype=torch.int32, device=device)
+        self.partial = torch.empty(world * T, H, dtype=torch.float32, device=device)
+        self.received = torch.empty(world, T, H, dtype=torch.float32, device=device)
+
+
+class ExpertParallelBlock:
+    """One rank's share of an expert-parallel MoE block (see the module docstring)."""
+
+    def __init__(self, weights: BlockWeights, config: Optional[MoeConfig] = None, *, expert_begin: int,
+                 num_local: int, group=None, ops=None):
+        self.config = config or weights.config
+        if self.config.shared_inter:
+            raise MlxError("moe_ep_experts", 2, "the expert-parallel path has no shared expert")
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.expert_begin, self.num_local = expert_begin, num_local
+        self.ops = ops if ops is not None else CudaEpOps()
+        self.bound = self.ops.bind(weights, self.config)
+        self._buf: dict = {}
+
+    def buffers(self, T: int, device) -> _Buffers:
+        b = self._buf.get((T, str(device)))
+        if b is None:
+            c = self.config
+            b = _Buffers(T, c.hidden, c.top_k, self.world, device)
+            self._buf[(T, str(device))] = b
+        return b
+
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None, *, norm_weight=None,
+                eps: float = 1e-6, normed: Optional[torch.Tensor] = None, buffers: Optional[_Buffers] = None):
+        """out[T_r, H] = this rank's rows of the block applied to every rank's tokens.
+        With norm_weight, normed = RMSNorm(out) * norm_weight is written as well."""
+        c = self.config
+        if x.dim() != 2 or x.shape[1] != c.hidden or x.dtype != torch.bfloat16 or not x.is_contiguous():
+            raise MlxError("moe_ep_route", 1, f"x must be contiguous bf16 [T, {c.hidden}]")
+        T = x.shape[0]
+        b = buffers if buffers is not None else self.buffers(T, x.device)
+        if out is None:
+            out = torch.empty_like(x)
+        g = self.group
+        self.ops.route(self.bound, x, b.packed)
+        dist.all_gather_into_tensor(b.x_all.view(torch.uint8), x.view(torch.uint8), group=g)
+        dist.all_gather_into_tensor(b.packed_all, b.packed, group=g)
+        self.ops.experts(self.bound, b.x_all, b.packed_all, self.expert_begin, self.num_local, b.partial)
+        dist.all_to_all_single(b.received.view(-1), b.partial.view(-1), group=g)
+        self.ops.finish(b.received, self.world, out, norm_weight, eps, normed)
+        return out
+
+    __call__ = forward
+
+
+class ExpertParallelStack:
+    """h = x; for each layer l: if l > 0: h = RmsNorm_l(h); h = block_l(h), every block
+    expert-parallel; the RMSNorm runs fused into the previous block's finish step."""
+
+    def __init__(self, blocks: Sequence[ExpertParallelBlock], norm_weights: Sequence[Optional[torch.Tensor]],
+                 eps: float = 1e-6):
+        self.blocks, self.norm_weights, self.eps = list(blocks), list(norm_weights), eps
+        c0 = self.blocks[0].config
+        if any((b.config.hidden, b.config.top_k) != (c0.hidden, c0.top_k) for b in self.blocks):
+            raise MlxError("ExpertParallelStack", 1, "blocks must share hidden size and top_k")
+        self._h: dict = {}
+
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None):
+        T, H = x.shape
+        key = (T, str(x.device))
+        if key not in self._h:
+            self._h[key] = torch.empty_like(x)
+        h = self._h[key]
+        if out is None:
+            out = torch.empty_like(x)
+        buf = self.blocks[0].buffers(T, x.device)
+        cur = x
+        L = len(self.blocks)
+        for l, blk in enumerate(self.blocks):
+            last = l == L - 1
+            nw = None if last else self.norm_weights[l + 1]
+            normed = h if nw is not None else None
+            # x and out may alias: the block reads x (route, all-gather) before it writes out
+            blk.forward(cur, out, norm_weight=nw, eps=self.eps, normed=normed, buffers=buf)
+            cur = h if normed is not None else out
+        return out
+
+    __call__ = forward
+
+
+__all__ = ["expert_range", "local_weights", "CudaEpOps", "ExpertParallelBlock", "ExpertParallelStack"]

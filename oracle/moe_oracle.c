@@ -622,6 +622,12 @@ static void swiglu_bf16(const uint16_t* g, const uint16_t* u, int64_t n, uint16_
     }
 }
 
+int oracle_swiglu(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* h) {
+    if (n < 0) return -1;
+    swiglu_bf16(g, u, n, h);
+    return 0;
+}
+
 typedef struct {
     const uint16_t *y, *wsel, *ys, *gl;
     int k, has_shared, has_gate;

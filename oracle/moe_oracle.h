@@ -105,6 +105,9 @@ int oracle_group_by_expert(int64_t T, int k, int E, const uint32_t* idx, int32_t
 int oracle_rms_norm(const uint16_t* x, const uint16_t* w, float eps, int64_t rows, int64_t dim,
                     uint16_t* out, int nthreads);
 
+/* h = bf16(bf16(g * bf16(sigmoid(g))) * u) elementwise (the SwitchGLU activation). */
+int oracle_swiglu(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* h);
+
 int oracle_block_forward(const oracle_block_config* cfg, const oracle_block_weights* wt,
                          const uint16_t* x, int64_t T, uint16_t* out, uint32_t* idx_out,
                          uint16_t* weights_out, int nthreads);

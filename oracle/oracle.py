@@ -77,6 +77,7 @@ def lib():
                                       C.c_void_p, C.c_int]
         L.oracle_block_forward.argtypes = [C.POINTER(_Cfg), C.POINTER(_Wts), C.c_void_p, C.c_int64,
                                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+        L.oracle_swiglu.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]
         _lib = L
     return _lib
 
@@ -241,3 +242,78 @@ def stack_forward(blocks, norm_weights, x, eps=1e-6, nthreads=0):
             h = rms_norm(h, norm_weights[l], eps, nthreads)
         h, _, _ = block_forward(blk, h, nthreads)
     return h
+
+
+# ----------------------------------------------------------------------------------
+# Expert parallelism: the block split over ranks by expert range (the reference runs on
+# one device; this restates its combine, qwen3_moe_python_port.rs:471-472, with the
+# k-term fp32 sum split by rank and the ranks' partial sums added in rank order).
+# ----------------------------------------------------------------------------------
+
+def _f(bits):
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def _rbf(v):
+    """Round float32 values to bf16 and back (ties to even)."""
+    b = v.astype(np.float32).view(np.uint32)
+    r = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint32)
+    nan = np.isnan(v)
+    r[nan] = (b[nan] >> 16) | 0x40
+    return (r << 16).view(np.float32)
+
+
+def swiglu(g, u):
+    g = _c(g, np.uint16)
+    u = _c(u, np.uint16)
+    h = np.empty_like(g)
+    _check(lib().oracle_swiglu(_p(g), _p(u), g.size, _p(h)), "oracle_swiglu")
+    return h
+
+
+def pack_routing(idx, weights):
+    """[T, k] expert | bf16 weight << 16 (the expert-parallel routing record)."""
+    return (idx.astype(np.uint32) | (weights.astype(np.uint32) << 16)).astype(np.uint32)
+
+
+def ep_partials(block_local, x_all, packed_all, expert_begin, num_local, nthreads=0):
+    """partial[t] (float32) = sum over j in order, of the pairs whose expert lies in
+    [expert_begin, expert_begin + num_local), of bf16(y * w); block_local holds those
+    experts' gate/up/down ([num_local, N, K/8])."""
+    x_all = _c(x_all, np.uint16)
+    T, H = x_all.shape
+    k = packed_all.shape[1]
+    e = (packed_all & 0xFFFF).astype(np.int64) - expert_begin
+    w = (packed_all >> 16).astype(np.uint16)
+    local = (e >= 0) & (e < num_local)
+    flat = np.flatnonzero(local.reshape(-1))
+    partial = np.zeros((T, H), np.float32)
+    if flat.size == 0:
+        return partial
+    t = (flat // k).astype(np.uint32)
+    el = e.reshape(-1)[flat].astype(np.uint32)
+    b = block_local
+    g = gather_qmm(x_all, b.gate.w, b.gate.scales, b.gate.biases, el, lhs=t, nthreads=nthreads)
+    u = gather_qmm(x_all, b.up.w, b.up.scales, b.up.biases, el, lhs=t, nthreads=nthreads)
+    h = swiglu(g, u)
+    y = gather_qmm(h, b.down.w, b.down.scales, b.down.biases, el, x_repeat=1, nthreads=nthreads)
+    yf = _f(y)
+    wf = _f(w.reshape(-1)[flat])
+    j = flat % k
+    for jj in range(k):
+        sel = np.flatnonzero(j == jj)
+        if sel.size:
+            partial[t[sel]] = partial[t[sel]] + _rbf(yf[sel] * wf[sel, None])
+    return partial
+
+
+def ep_finish(received, norm_weight=None, eps=1e-6):
+    """out = bf16(sum over ranks in order of received[s]); with norm_weight also
+    rms_norm(out) (returns (out, normed))."""
+    acc = np.zeros(received.shape[1:], np.float32)
+    for s in range(received.shape[0]):
+        acc = acc + received[s].astype(np.float32)
+    b = acc.view(np.uint32)
+    out = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+    normed = rms_norm(out, norm_weight, eps) if norm_weight is not None else None
+    return out, normed
