@@ -292,7 +292,7 @@ enum Stage { kRouter = 0, kTopk, kGroup, kGateUp, kDown, kSharedGateUp, kSharedD
 // With `packed`, routing writes [T, k] expert | bf16(weight) << 16 there and stops
 // before the grouping (the expert-parallel route).
 int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* w, const void* x, int64_t T,
-              const BlockWs& ws, cudaEvent_t* ev = nullptr, uint32_t* packed = nullptr) {
+              const BlockWs& ws, cudaEvent_t* ev = nullptr, uint32_t* packed = nullptr, int tc_min_rows = 0) {
   const int E = c->num_experts;
   const bool gate_row = c->shared_inter > 0 && c->has_shared_gate;
   moe::RouterArgs ra{};
@@ -344,6 +344,7 @@ int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* 
   ga.inv = ws.inv;
   ga.tile_start = ws.tile_start;
   ga.tile_rows = moe::kTcTileRows;
+  ga.tc_min_rows = tc_min_rows;
   MOE_MARK(ev, kGroup, ctx->stream);
   MOE_CUDA(ctx, moe::launch_group(ga, ctx->stream));
   return MOE_OK;
@@ -357,6 +358,47 @@ bool use_tc(int64_t rows, int64_t experts, int N, int K) {
   if (v && v[0] == '0') return false;
   if (v && v[0] == '1') return true;
   return rows >= 32 * experts;
+}
+
+// Routed experts: each expert takes the path its own row count calls for, decided on
+// the device. Experts with at least kTcMinRows rows run on the tcgen05 GEMM (the
+// grouping gives only them tiles); the others on the GEMV, which skips the large ones.
+// MOE_B200_TC=0 puts every expert on the GEMV, =1 every expert on tcgen05.
+constexpr int kTcMinRows = 32;
+struct ExpertPlan {
+  bool tc_gu = false, tc_dn = false;      // launch the tcgen05 kernel
+  bool gemv_gu = true, gemv_dn = true;    // launch the GEMV
+  int min_rows = 0;                       // tile threshold of the grouping
+  int gemv_skip_gu = 0, gemv_skip_dn = 0; // GEMV max_expert_rows
+  int max_tiles = 0;                      // tcgen05 grid.y
+};
+
+ExpertPlan plan_experts(int64_t P, int E, int I, int H) {
+  ExpertPlan p;
+  const bool shape_gu = I % 128 == 0 && H % 64 == 0, shape_dn = H % 128 == 0 && I % 64 == 0;
+  const char* v = std::getenv("MOE_B200_TC");
+  if (v && v[0] == '0') return p;
+  if (v && v[0] == '1') {
+    p.tc_gu = shape_gu;
+    p.tc_dn = shape_dn;
+    p.gemv_gu = !shape_gu;
+    p.gemv_dn = !shape_dn;
+  } else if (P >= (int64_t)4 * kTcMinRows * E) {
+    // prefill: nearly every expert is large, all go to tcgen05 (no GEMV launch)
+    p.tc_gu = shape_gu;
+    p.tc_dn = shape_dn;
+    p.gemv_gu = !shape_gu;
+    p.gemv_dn = !shape_dn;
+  } else if (P >= kTcMinRows) {
+    p.tc_gu = shape_gu;
+    p.tc_dn = shape_dn;
+    p.min_rows = kTcMinRows;
+    p.gemv_skip_gu = shape_gu ? kTcMinRows : 0;
+    p.gemv_skip_dn = shape_dn ? kTcMinRows : 0;
+  }
+  const int64_t big = p.min_rows ? std::min<int64_t>(E, P / p.min_rows) : std::min<int64_t>(E, P);
+  p.max_tiles = (int)(P / moe::kTcTileRows + big + 1);
+  return p;
 }
 
 moe::QgemvArgs qgemv_args(const moe_qweight& m0, const moe_qweight* m1, int N, int K) {
@@ -394,17 +436,15 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   rc = ensure_scratch(ctx, carve_block(nullptr, cfg, T).bytes);
   if (rc) return rc;
   BlockWs ws = carve_block(ctx->scratch, cfg, T);
-  rc = run_route(ctx, cfg, wts, x, T, ws, ev);
-  if (rc) return rc;
-
   const int E = cfg->num_experts, H = cfg->hidden, I = cfg->moe_inter, k = cfg->top_k;
   const int64_t P = T * k;
+  const ExpertPlan plan = plan_experts(P, E, I, H);
+  rc = run_route(ctx, cfg, wts, x, T, ws, ev, nullptr, plan.min_rows);
+  if (rc) return rc;
+
   const int slots = (int)std::min<int64_t>(P, E);
   // Token chunk of the decode GEMV: 8 rows (an expert with more rows takes more chunks).
   const int max_rows = 8;
-
-  const bool tc_gu = use_tc(P, E, I, H), tc_dn = use_tc(P, E, H, I);
-  const int max_tiles = (int)(P / moe::kTcTileRows + std::min<int64_t>(E, P) + 1);
   // SwitchGLU gate/up + SiLU*up over grouped rows (x row = pair / k).
   moe::QgemvArgs gu = qgemv_args(wts->gate, &wts->up, I, H);
   gu.x = static_cast<const uint16_t*>(x);
@@ -417,10 +457,12 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   gu.out = ws.hbuf;
   gu.out_mode = 0;
   MOE_MARK(ev, kGateUp, ctx->stream);
-  if (tc_gu) {
-    moe::TcGemmArgs ta{gu, ws.tile_start, E, max_tiles, ws.status};
+  if (plan.tc_gu) {
+    moe::TcGemmArgs ta{gu, ws.tile_start, E, plan.max_tiles, ws.status};
     MOE_CUDA(ctx, moe::launch_tc_gemm(ta, true, ctx->stream));
-  } else {
+  }
+  if (plan.gemv_gu) {
+    gu.max_expert_rows = plan.gemv_skip_gu;
     MOE_CUDA(ctx, moe::launch_qgemv(gu, true, slots, max_rows, ctx->stream));
   }
 
@@ -435,10 +477,12 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   dn.out = ws.ybuf;
   dn.out_mode = 0;
   MOE_MARK(ev, kDown, ctx->stream);
-  if (tc_dn) {
-    moe::TcGemmArgs ta{dn, ws.tile_start, E, max_tiles, ws.status};
+  if (plan.tc_dn) {
+    moe::TcGemmArgs ta{dn, ws.tile_start, E, plan.max_tiles, ws.status};
     MOE_CUDA(ctx, moe::launch_tc_gemm(ta, false, ctx->stream));
-  } else {
+  }
+  if (plan.gemv_dn) {
+    dn.max_expert_rows = plan.gemv_skip_dn;
     MOE_CUDA(ctx, moe::launch_qgemv(dn, false, slots, max_rows, ctx->stream));
   }
 
@@ -762,15 +806,17 @@ int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_we
   ga.n_active = ws.n_active;
   ga.perm = ws.perm;
   ga.inv = ws.inv;
+  // Path choice per expert as in moe_block_forward, on the expected rows per expert of
+  // all pairs over all E experts; the grids cover every local pair in the worst case
+  // and idle CTAs leave at once.
+  ExpertPlan plan = plan_experts(P, E, I, H);
+  plan.max_tiles = (int)(P / moe::kTcTileRows +
+                         std::min<int64_t>(El, plan.min_rows ? P / plan.min_rows : P) + 1);
   ga.tile_start = ws.tile_start;
   ga.tile_rows = moe::kTcTileRows;
+  ga.tc_min_rows = plan.min_rows;
   MOE_CUDA(ctx, moe::launch_group(ga, ctx->stream));
-
-  // Path choice on the expected rows per expert (all pairs over all E experts); the
-  // grids cover every local pair in the worst case and idle CTAs leave at once.
-  const bool tc_gu = use_tc(P, E, I, H), tc_dn = use_tc(P, E, H, I);
   const int slots = (int)std::min<int64_t>(P, El);
-  const int max_tiles = (int)(P / moe::kTcTileRows + std::min<int64_t>(El, P) + 1);
   moe::QgemvArgs gu = qgemv_args(wts->gate, &wts->up, I, H);
   gu.x = static_cast<const uint16_t*>(x_all);
   gu.x_mode = 1;
@@ -780,10 +826,12 @@ int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_we
   gu.active = ws.active;
   gu.n_active = ws.n_active;
   gu.out = ws.hbuf;
-  if (tc_gu) {
-    moe::TcGemmArgs ta{gu, ws.tile_start, El, max_tiles, ws.status};
+  if (plan.tc_gu) {
+    moe::TcGemmArgs ta{gu, ws.tile_start, El, plan.max_tiles, ws.status};
     MOE_CUDA(ctx, moe::launch_tc_gemm(ta, true, ctx->stream));
-  } else {
+  }
+  if (plan.gemv_gu) {
+    gu.max_expert_rows = plan.gemv_skip_gu;
     MOE_CUDA(ctx, moe::launch_qgemv(gu, true, slots, 8, ctx->stream));
   }
   moe::QgemvArgs dn = qgemv_args(wts->down, nullptr, H, I);
@@ -794,10 +842,12 @@ int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_we
   dn.active = ws.active;
   dn.n_active = ws.n_active;
   dn.out = ws.ybuf;
-  if (tc_dn) {
-    moe::TcGemmArgs ta{dn, ws.tile_start, El, max_tiles, ws.status};
+  if (plan.tc_dn) {
+    moe::TcGemmArgs ta{dn, ws.tile_start, El, plan.max_tiles, ws.status};
     MOE_CUDA(ctx, moe::launch_tc_gemm(ta, false, ctx->stream));
-  } else {
+  }
+  if (plan.gemv_dn) {
+    dn.max_expert_rows = plan.gemv_skip_dn;
     MOE_CUDA(ctx, moe::launch_qgemv(dn, false, slots, 8, ctx->stream));
   }
   moe::EpPartialArgs pa{};

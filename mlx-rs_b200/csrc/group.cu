@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(1024) group_small_kernel(GroupArgs a) {
   const int32_t base = block_exclusive_scan(tid < E ? tot : 0, warp_tot, nullptr);
   const int32_t arank = block_exclusive_scan((tid < E && tot > 0) ? 1 : 0, warp_tot, &n_act);
   if (a.tile_start) {
-    const int32_t nt = tid < E ? (tot + a.tile_rows - 1) / a.tile_rows : 0;
+    const int32_t nt = (tid < E && tot >= a.tc_min_rows) ? (tot + a.tile_rows - 1) / a.tile_rows : 0;
     const int32_t tbase = block_exclusive_scan(nt, warp_tot, nullptr);
     if (tid <= E) a.tile_start[tid] = tbase;
   }
@@ -210,7 +210,8 @@ __global__ void __launch_bounds__(1024) group_scan_kernel(GroupArgs a) {
       int32_t run = 0;
       for (int e = 0; e < a.E; ++e) {
         a.tile_start[e] = run;
-        run += (a.offsets[e + 1] - a.offsets[e] + a.tile_rows - 1) / a.tile_rows;
+        const int32_t cnt = a.offsets[e + 1] - a.offsets[e];
+        if (cnt >= a.tc_min_rows) run += (cnt + a.tile_rows - 1) / a.tile_rows;
       }
       a.tile_start[a.E] = run;
     }

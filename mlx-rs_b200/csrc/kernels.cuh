@@ -73,6 +73,7 @@ struct GroupArgs {
   uint32_t* inv;    // [P] p -> pos, may be null
   int32_t* tile_start;  // [E + 1] exclusive prefix of ceil(count_e / tile_rows), may be null
   int tile_rows;
+  int tc_min_rows;      // experts with fewer pairs get no tiles (0: every expert)
 };
 
 // Grouped quantized GEMV/GEMM over expert-grouped rows (tensor cores via mma.sync,
@@ -96,6 +97,7 @@ struct QgemvArgs {
   int N, K;
   uint16_t* out;            // [rows, N] bf16
   int out_mode;             // 0: row = pos, 1: row = perm[pos]
+  int max_expert_rows;      // experts with this many rows or more are skipped (0: none)
 };
 
 struct CombineArgs {

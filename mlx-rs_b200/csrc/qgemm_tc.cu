@@ -6,18 +6,20 @@
 //
 // One CTA computes D[128 weight rows x n tokens] = W_tile . X_tile^T over the whole K
 // for one expert and one tile of up to 256 of its (grouped) token rows:
-//   * warps 0-3 (128 threads) are producers: per K step of 64 (one quantization group)
-//     they load the packed int4 rows, dequantise them to bf16 (w = RN_bf16(s*q + b), the
-//     value MLX's GPU qmm computes into threadgroup memory) and store them as the A tile,
-//     and copy the token rows with cp.async as the B tile; both tiles are K-major with
-//     the 128-byte swizzle the tensor core reads;
-//   * warp 4 allocates tensor memory and, from one lane, issues tcgen05.mma
+//   * warps 0-7 (256 threads) are producers: per K step of 64 (one quantization group)
+//     thread p loads 32 packed int4 elements of weight row p/2 (half p%2 of the group),
+//     dequantises them to bf16 (w = RN_bf16(s*q + b), the value MLX's GPU qmm computes
+//     into threadgroup memory) and stores them into the A tile, and copies its share of
+//     the token rows with cp.async into the B tile; both tiles are K-major with the
+//     128-byte swizzle the tensor core reads;
+//   * warp 8 allocates tensor memory and, from one lane, issues tcgen05.mma
 //     (kind::f16, bf16 x bf16 -> fp32, M=128, N=n rounded up to 16, K=16 per instruction)
 //     accumulating in TMEM; tcgen05.commit on an mbarrier frees each stage;
 //   * after the last stage the producer warps read the accumulators back with
-//     tcgen05.ld (warp w owns TMEM lanes 32w..32w+31 = weight rows) and write bf16
-//     outputs; in the gated form the gate and up accumulators (TMEM columns 0 and 256)
-//     are combined by SwiGLU in registers.
+//     tcgen05.ld (warp w owns TMEM lanes 32(w%4).. = weight rows, and every other block
+//     of 32 token columns by w/4); in the gated form the gate and up accumulators (TMEM
+//     columns 0 and 256) are combined by SwiGLU in registers. Each warp transposes its
+//     32 x 32 tile through shared memory so that the outputs leave as 16-byte stores.
 // The shared-memory ring has kStages stages guarded by full/empty mbarriers. Every
 // mbarrier wait is bounded; on expiry the CTA records a status code and drains out.
 // No TMA and no cluster multicast are used.
@@ -33,7 +35,8 @@ constexpr int kBN = kTcTileRows;           // max tokens per CTA (MMA N)
 constexpr int kBK = 64;                    // K per stage
 constexpr int kATileBytes = kBM * kBK * 2;   // 16 KB
 constexpr int kBTileBytes = kBN * kBK * 2;   // 32 KB
-constexpr int kProducers = 128;
+constexpr int kProducers = 256;
+constexpr int kMmaWarp = kProducers / 32;
 constexpr int kThreads = kProducers + 32;
 constexpr uint64_t kWaitLimitNs = 200ull * 1000 * 1000;  // bound of one mbarrier wait (200 ms)
 
@@ -169,6 +172,12 @@ MOE_DEV uint4 dequant8(uint32_t w, uint32_t s2, uint32_t b2) {
   return o;
 }
 
+MOE_DEV uint4 lds_v4(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+
 // Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled K-major tile.
 MOE_DEV uint32_t sw128_off(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
@@ -241,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
     mbar_init(bar_done, 1);
   }
   for (int i = tid; i < kBN; i += kThreads) xrow_s[i] = i < ntok ? (int32_t)rm.xrow(tbeg + i) : -1;
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
                  "r"(C::kTmemCols)
                  : "memory");
@@ -252,46 +261,42 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < 4) {
+  if (warp < kMmaWarp) {
     // ================= producers (then epilogue) =================
-    const int p = tid;                 // 0..127
-    const int half = p & 1;            // which 32 elements of the row's 64
-    const int rsub = p >> 1;           // rows rsub and rsub + 64
-    const uint32_t* wrow[C::kMats][2];
-    const uint16_t* srow[C::kMats][2];
-    const uint16_t* brow[C::kMats][2];
+    const int p = tid;          // 0..255
+    const int half = p & 1;     // which 32 elements of the row's group of 64
+    const int row = p >> 1;     // weight row within the tile
+    const uint32_t* wrow[C::kMats];
+    const uint16_t* srow[C::kMats];
+    const uint16_t* brow[C::kMats];
 #pragma unroll
-    for (int m = 0; m < C::kMats; ++m)
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const size_t row = (size_t)e * N + n0 + rsub + 64 * i;
-        const uint32_t* W = m ? a.w1 : a.w0;
-        const uint16_t* S = m ? a.s1 : a.s0;
-        const uint16_t* B = m ? a.b1 : a.b0;
-        wrow[m][i] = W + row * wpr + half * 4;
-        srow[m][i] = S + row * G;
-        brow[m][i] = B ? B + row * G : nullptr;
-      }
-    // register ring of packed weights + scales, 2 stages ahead
-    uint4 wr[3][C::kMats][2];
-    uint32_t sr[3][C::kMats][2];  // (s | b << 16)
+    for (int m = 0; m < C::kMats; ++m) {
+      const size_t grow = (size_t)e * N + n0 + row;
+      const uint32_t* W = m ? a.w1 : a.w0;
+      const uint16_t* S = m ? a.s1 : a.s0;
+      const uint16_t* B = m ? a.b1 : a.b0;
+      wrow[m] = W + grow * wpr + half * 4;
+      srow[m] = S + grow * G;
+      brow[m] = B ? B + grow * G : nullptr;
+    }
+    // register ring of packed weights + (scale | bias << 16), 2 stages ahead
+    uint4 wr[3][C::kMats];
+    uint32_t sr[3][C::kMats];
     auto load_w = [&](int slot3, int kk) {
       if (kk < G) {
 #pragma unroll
-        for (int m = 0; m < C::kMats; ++m)
-#pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            wr[slot3][m][i] = __ldg(reinterpret_cast<const uint4*>(wrow[m][i] + (size_t)kk * 8));
-            const uint32_t sv = __ldg(srow[m][i] + kk);
-            const uint32_t bv = brow[m][i] ? __ldg(brow[m][i] + kk) : 0u;
-            sr[slot3][m][i] = sv | (bv << 16);
-          }
+        for (int m = 0; m < C::kMats; ++m) {
+          wr[slot3][m] = __ldg(reinterpret_cast<const uint4*>(wrow[m] + (size_t)kk * 8));
+          const uint32_t sv = __ldg(srow[m] + kk);
+          const uint32_t bv = brow[m] ? __ldg(brow[m] + kk) : 0u;
+          sr[slot3][m] = sv | (bv << 16);
+        }
       }
     };
     auto issue_b = [&](int kk) {
       const uint32_t bt = sbase + (kk % C::kStages) * C::kStageBytes + C::kMats * kATileBytes;
-      // 256 rows x 8 chunks; this thread: chunks q = p + 128 i
-#pragma unroll 4
+      // 256 rows x 8 chunks of 16 bytes; this thread: chunks q = p + 256 i
+#pragma unroll
       for (int i = 0; i < kBN * 8 / kProducers; ++i) {
         const int q = p + kProducers * i;
         const int r = q >> 3, c = q & 7;
@@ -320,23 +325,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
           const uint32_t st = sbase + s * C::kStageBytes;
           // dequantise A(kk) into stage s (freed: its empty barrier was awaited when B(kk) was issued)
 #pragma unroll
-          for (int m = 0; m < C::kMats; ++m)
+          for (int m = 0; m < C::kMats; ++m) {
+            const uint32_t sv = sr[r3][m] & 0xffffu, bv = sr[r3][m] >> 16;
+            const uint32_t s2 = sv | (sv << 16), b2 = bv | (bv << 16);
+            const uint4 wv = wr[r3][m];
+            const uint32_t ws[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              const int row = rsub + 64 * i;
-              const uint32_t sv = sr[r3][m][i] & 0xffffu, bv = sr[r3][m][i] >> 16;
-              const uint32_t s2 = sv | (sv << 16), b2 = bv | (bv << 16);
-              const uint4 wv = wr[r3][m][i];
-              const uint32_t ws[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint4 o = dequant8(ws[j], s2, b2);
-                const uint32_t dst = st + m * kATileBytes + sw128_off(row, half * 4 + j);
-                asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(dst), "r"(o.x), "r"(o.y), "r"(o.z),
-                             "r"(o.w)
-                             : "memory");
-              }
+            for (int j = 0; j < 4; ++j) {
+              const uint4 o = dequant8(ws[j], s2, b2);
+              const uint32_t dst = st + m * kATileBytes + sw128_off(row, half * 4 + j);
+              asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(dst), "r"(o.x), "r"(o.y), "r"(o.z),
+                           "r"(o.w)
+                           : "memory");
             }
+          }
           load_w((r3 + 2) % 3, kk + 2);
           // B(kk) landed: at most LA-1 newer groups may still be pending
           cp_wait<LA - 1>();
@@ -365,9 +367,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
     tc_fence_after();
     pdl_trigger();
     if (done_ok) {
-      const int row = n0 + 32 * warp + lane;  // TMEM lane = row within the tile
-      const uint32_t tl = tmem + ((uint32_t)(32 * warp) << 16);
-      for (int c0 = 0; c0 < nmma; c0 += 32) {
+      // Every MMA has completed, so the stage buffers are free: each warp transposes its
+      // 32 rows x 32 tokens tile through 2 KB of stage 0.
+      const int quad = warp & 3;                    // TMEM lanes 32*quad.. (weight rows)
+      const uint32_t tl = tmem + ((uint32_t)(32 * quad) << 16);
+      unsigned char* tile = smem + warp * 2048;     // [32 tokens][32 rows] bf16
+      const uint32_t tile_s = sbase + warp * 2048;
+      for (int c0 = 32 * (warp >> 2); c0 < nmma; c0 += 64) {
         uint32_t g[32];
         tmem_ld32(tl + c0, g);
         if (GATED) {
@@ -375,28 +381,32 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
           tmem_ld32(tl + 256 + c0, u);
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const int t = c0 + j;
-            if (t < ntok) {
-              const int64_t pos = tbeg + t;
-              const int64_t orow = a.out_mode == 0 ? pos : rm.orig(pos);
-              a.out[(size_t)orow * N + row] = swiglu_bf16(rbf(__uint_as_float(g[j])), rbf(__uint_as_float(u[j])));
-            }
+            const uint16_t v = swiglu_bf16(rbf(__uint_as_float(g[j])), rbf(__uint_as_float(u[j])));
+            *reinterpret_cast<uint16_t*>(tile + j * 64 + lane * 2) = v;
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int t = c0 + j;
-            if (t < ntok) {
-              const int64_t pos = tbeg + t;
-              const int64_t orow = a.out_mode == 0 ? pos : rm.orig(pos);
-              a.out[(size_t)orow * N + row] = f2bf(__uint_as_float(g[j]));
-            }
+          for (int j = 0; j < 32; ++j)
+            *reinterpret_cast<uint16_t*>(tile + j * 64 + lane * 2) = f2bf(__uint_as_float(g[j]));
+        }
+        __syncwarp();
+        // token row t of the tile = 64 bytes = 4 x 16 bytes; lane -> (t = lane/4 + 8i, piece lane%4)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int t = (lane >> 2) + 8 * i;
+          const int tok = c0 + t;
+          if (tok < ntok) {
+            const uint4 v = lds_v4(tile_s + t * 64 + (lane & 3) * 16);
+            const int64_t pos = tbeg + tok;
+            const int64_t orow = a.out_mode == 0 ? pos : rm.orig(pos);
+            *reinterpret_cast<uint4*>(a.out + (size_t)orow * N + n0 + 32 * quad + (lane & 3) * 8) = v;
           }
         }
+        __syncwarp();
       }
     }
   } else if (lane == 0) {
-    // ================= MMA issuer (warp 4, one lane) =================
+    // ================= MMA issuer (warp 8, one lane) =================
     const uint32_t idesc = idesc_bf16(nmma);
     bool ok = true;
     for (int kk = 0; kk < G; ++kk) {
@@ -427,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
   tc_fence_before();
   __syncthreads();
   if (abort_flag && tid == 0 && ta.status) atomicOr(ta.status, abort_flag);
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(C::kTmemCols) : "memory");
   }

@@ -129,6 +129,7 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
   const int64_t row_begin = a.offsets ? a.offsets[e] : 0;
   const int64_t row_end = a.offsets ? a.offsets[e + 1] : a.n_identity;
   if (row_end <= row_begin) return;
+  if (a.max_expert_rows && row_end - row_begin >= a.max_expert_rows) return;  // the tensor-core kernel's
   const int K = a.K, N = a.N, G = K >> 6, wpr = K >> 3;
   const int r0 = ut * ROWS;
   const bool unit_live = ut < units_per_expert && r0 < N;  // warp-uniform; the warp still stages
