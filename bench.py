@@ -338,6 +338,40 @@ def tensor_roofline(name, flops, launch_ms, extra=None):
     return r
 
 
+def capture_graph(fn, static_x, dev, world):
+    """CUDA graph of fn(static_x) (collectives included), or None; every rank ends with
+    the same choice (a capture that failed on any rank is dropped on all)."""
+    import torch
+    import torch.distributed as dist
+    cur = torch.cuda.current_stream(dev)
+    graph, err = None, None
+    try:
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(cur)
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                fn(static_x)
+        cur.wait_stream(s)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn(static_x)
+        torch.cuda.synchronize()
+    except Exception as e:
+        graph, err = None, f"{type(e).__name__}: {str(e)[:120]}"
+        torch.cuda.synchronize()
+    if world > 1:
+        ok = torch.tensor([0 if graph is None else 1], device=dev, dtype=torch.int32)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if int(ok.item()) == 0:
+            graph = None
+            err = err or "capture failed on another rank"
+    if graph is not None:
+        graph.replay()
+        torch.cuda.synchronize()
+    return graph, ("cuda_graph" if graph is not None else f"eager (graph capture failed: {err})")
+
+
 def group_launches(P, E):
     return 1 if (P <= 32768 and E <= 512) else 3
 
@@ -577,11 +611,21 @@ def run_ep_block(args, world, rank, local, dev):
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
+    static_x = torch.empty_like(xs[0])
+    static_x.copy_(xs[0])
+    graph, mode = (None, "eager") if args.no_graph else capture_graph(lambda x: blk.forward(x, out), static_x,
+                                                                        dev, world)
+
     def step(i):
         a, b = events()
         flush.zero_()
-        a.record(stream)
-        blk.forward(xs[i % pool], out)
+        if graph is not None:
+            static_x.copy_(xs[i % pool])
+            a.record(stream)
+            graph.replay()
+        else:
+            a.record(stream)
+            blk.forward(xs[i % pool], out)
         b.record(stream)
         return a, b
 
@@ -601,6 +645,7 @@ def run_ep_block(args, world, rank, local, dev):
                             {"stage_ms": stage_ms, "local_experts_touched": n_act})
     roof["rank"] = 0  # rank 0's own experts and their device time
     e2e = e2e_run(args, lambda xd: blk.forward(xd, out), xs_host, (T, H), dev, timer)
+    del graph  # holds NCCL work: released before the process group is destroyed
     launches = 4 + 2 + group_launches(P_all, n)
     return {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -610,7 +655,7 @@ def run_ep_block(args, world, rank, local, dev):
                    "global_batch": T * world, "seq_len": 1, "parallelism": f"ep{world}",
                    "experts": cfg.num_experts, "experts_per_gpu": n, "top_k": cfg.top_k, "hidden": H,
                    "moe_inter": cfg.moe_inter, "collectives": "NCCL all_gather x2 (dispatch), all_to_all (combine)",
-                   "l2": "flushed (256 MiB write) before every timed step", "launch": "eager",
+                   "l2": "flushed (256 MiB write) before every timed step", "launch": mode,
                    "clock_window": "nvidia-smi every 200 ms across 0.6 s of untimed steps, the timed steps, 0.6 s more"},
         "roofline": roof,
         "cpu_baseline": None,
@@ -663,24 +708,10 @@ def run_stack(args, world, rank, local, dev):
     def fwd(x):
         return stack.forward(x, out) if world > 1 else out.copy_(stack.forward(x))
 
-    # one GPU: the whole stack replays from a CUDA graph; expert-parallel: eager launches
-    graph, mode = None, "eager"
+    # the whole stack (collectives included) replays from one CUDA graph
     static_x = torch.empty_like(xs[0])
-    if world == 1 and not args.no_graph:
-        try:
-            for i in range(2):
-                fwd(xs[i])
-            torch.cuda.synchronize()
-            static_x.copy_(xs[0])
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                fwd(static_x)
-            graph.replay()
-            torch.cuda.synchronize()
-            mode = "cuda_graph"
-        except Exception as e:
-            graph, mode = None, f"eager (graph capture failed: {type(e).__name__})"
-            torch.cuda.synchronize()
+    static_x.copy_(xs[0])
+    graph, mode = (None, "eager") if args.no_graph else capture_graph(fwd, static_x, dev, world)
 
     def step(i):
         a, b = events()
@@ -723,6 +754,7 @@ def run_stack(args, world, rank, local, dev):
 
     xs_host = [S.bf16_tensor_to_bits(x) for x in xs[:2]]
     e2e = e2e_run(args, fwd, xs_host, (T_r, H), dev, timer)
+    del graph  # holds NCCL work: released before the process group is destroyed
     cpu = None
     if rank == 0 and world == 1:
         bw0 = S.host_block(cfg, 1)

@@ -28,7 +28,6 @@ struct moe_ctx {
 
 namespace {
 
-constexpr int kGroupSeg = 1024;  // pairs per segment of the grouping sort
 
 int fail(moe_ctx* ctx, int code, const char* fmt, ...) {
   char buf[512];
@@ -136,7 +135,7 @@ BlockWs carve_block(void* base, const moe_block_config* c, int64_t T) {
   Carve cv(base);
   BlockWs w{};
   const int64_t E = c->num_experts, P = T * c->top_k;
-  const int64_t nseg = std::max<int64_t>(1, (P + kGroupSeg - 1) / kGroupSeg);
+  const int64_t nseg = std::max<int64_t>(1, (P + moe::group_seg(P, (int)E) - 1) / moe::group_seg(P, (int)E));
   w.status = cv.take<int32_t>(64);  // first, at a fixed offset; zeroed when allocated
   w.logits = cv.take<uint16_t>(T * (E + 1));
   w.idx = cv.take<uint32_t>(P);
@@ -264,7 +263,7 @@ EpWs carve_ep(void* base, const moe_block_config* c, int64_t T, int El) {
   Carve cv(base);
   EpWs w{};
   const int64_t P = T * c->top_k;
-  const int64_t nseg = std::max<int64_t>(1, (P + kGroupSeg - 1) / kGroupSeg);
+  const int64_t nseg = std::max<int64_t>(1, (P + moe::group_seg(P, El) - 1) / moe::group_seg(P, El));
   w.status = cv.take<int32_t>(64);  // first, at the fixed offset every workspace shares
   w.hist = cv.take<int32_t>(nseg * El);
   w.segbase = cv.take<int32_t>(nseg * El);
@@ -333,8 +332,8 @@ int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* 
   ga.key = ws.idx;
   ga.P = T * c->top_k;
   ga.E = E;
-  ga.seg = kGroupSeg;
-  ga.nseg = (int)std::max<int64_t>(1, (ga.P + kGroupSeg - 1) / kGroupSeg);
+  ga.seg = moe::group_seg(ga.P, E);
+  ga.nseg = (int)std::max<int64_t>(1, (ga.P + ga.seg - 1) / ga.seg);
   ga.hist = ws.hist;
   ga.segbase = ws.segbase;
   ga.offsets = ws.offsets;
@@ -443,8 +442,8 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   if (rc) return rc;
 
   const int slots = (int)std::min<int64_t>(P, E);
-  // Token chunk of the decode GEMV: 8 rows (an expert with more rows takes more chunks).
-  const int max_rows = 8;
+  // Expected rows per expert: how many tokens one GEMV pass over the weights serves.
+  const int rows_pe = (int)std::min<int64_t>((P + E - 1) / E, 1 << 20);
   // SwitchGLU gate/up + SiLU*up over grouped rows (x row = pair / k).
   moe::QgemvArgs gu = qgemv_args(wts->gate, &wts->up, I, H);
   gu.x = static_cast<const uint16_t*>(x);
@@ -457,13 +456,15 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   gu.out = ws.hbuf;
   gu.out_mode = 0;
   MOE_MARK(ev, kGateUp, ctx->stream);
+  // GEMV first: at decode sizes it carries the work, and the (mostly idle) tcgen05
+  // launch behind it overlaps its tail under programmatic dependent launch.
+  if (plan.gemv_gu) {
+    gu.max_expert_rows = plan.gemv_skip_gu;
+    MOE_CUDA(ctx, moe::launch_qgemv(gu, true, slots, rows_pe, ctx->stream));
+  }
   if (plan.tc_gu) {
     moe::TcGemmArgs ta{gu, ws.tile_start, E, plan.max_tiles, ws.status};
     MOE_CUDA(ctx, moe::launch_tc_gemm(ta, true, ctx->stream));
-  }
-  if (plan.gemv_gu) {
-    gu.max_expert_rows = plan.gemv_skip_gu;
-    MOE_CUDA(ctx, moe::launch_qgemv(gu, true, slots, max_rows, ctx->stream));
   }
 
   // down projection over the same grouped rows.
@@ -477,13 +478,13 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   dn.out = ws.ybuf;
   dn.out_mode = 0;
   MOE_MARK(ev, kDown, ctx->stream);
+  if (plan.gemv_dn) {
+    dn.max_expert_rows = plan.gemv_skip_dn;
+    MOE_CUDA(ctx, moe::launch_qgemv(dn, false, slots, rows_pe, ctx->stream));
+  }
   if (plan.tc_dn) {
     moe::TcGemmArgs ta{dn, ws.tile_start, E, plan.max_tiles, ws.status};
     MOE_CUDA(ctx, moe::launch_tc_gemm(ta, false, ctx->stream));
-  }
-  if (plan.gemv_dn) {
-    dn.max_expert_rows = plan.gemv_skip_dn;
-    MOE_CUDA(ctx, moe::launch_qgemv(dn, false, slots, max_rows, ctx->stream));
   }
 
   const bool shared = cfg->shared_inter > 0;
@@ -504,7 +505,7 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
       moe::TcGemmArgs ta{sgu, nullptr, 1, stiles, ws.status};
       MOE_CUDA(ctx, moe::launch_tc_gemm(ta, true, ctx->stream));
     } else {
-      MOE_CUDA(ctx, moe::launch_qgemv(sgu, true, 1, max_rows, ctx->stream));
+      MOE_CUDA(ctx, moe::launch_qgemv(sgu, true, 1, (int)T, ctx->stream));
     }
     moe::QgemvArgs sdn = qgemv_args(wts->shared_down, nullptr, H, Is);
     sdn.x = ws.hs;
@@ -516,7 +517,7 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
       moe::TcGemmArgs ta{sdn, nullptr, 1, stiles, ws.status};
       MOE_CUDA(ctx, moe::launch_tc_gemm(ta, false, ctx->stream));
     } else {
-      MOE_CUDA(ctx, moe::launch_qgemv(sdn, false, 1, max_rows, ctx->stream));
+      MOE_CUDA(ctx, moe::launch_qgemv(sdn, false, 1, (int)T, ctx->stream));
     }
   }
 
@@ -602,7 +603,7 @@ int moe_quantized_matmul(moe_ctx* ctx, const void* x, int64_t M, int64_t K, cons
   q.x_mode = 0;
   q.n_identity = (int)M;
   q.out = static_cast<uint16_t*>(out);
-  MOE_CUDA(ctx, moe::launch_qgemv(q, false, 1, (int)std::min<int64_t>(M, 16), ctx->stream));
+  MOE_CUDA(ctx, moe::launch_qgemv(q, false, 1, (int)std::min<int64_t>(M, 1 << 20), ctx->stream));
   return MOE_OK;
 }
 
@@ -628,7 +629,8 @@ int moe_gather_qmm(moe_ctx* ctx, const void* x, int64_t x_rows, int64_t K, int64
   if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
 
   const int E = (int)num_experts;
-  const int64_t nseg = std::max<int64_t>(1, (batch + kGroupSeg - 1) / kGroupSeg);
+  const int seg = moe::group_seg(batch, E);
+  const int64_t nseg = std::max<int64_t>(1, (batch + seg - 1) / seg);
   Carve size_only(nullptr);
   size_only.take<int32_t>(nseg * E);
   size_only.take<int32_t>(nseg * E);
@@ -643,7 +645,7 @@ int moe_gather_qmm(moe_ctx* ctx, const void* x, int64_t x_rows, int64_t K, int64
   ga.key = rhs_indices;
   ga.P = batch;
   ga.E = E;
-  ga.seg = kGroupSeg;
+  ga.seg = seg;
   ga.nseg = (int)nseg;
   ga.hist = cv.take<int32_t>(nseg * E);
   ga.segbase = cv.take<int32_t>(nseg * E);
@@ -667,7 +669,7 @@ int moe_gather_qmm(moe_ctx* ctx, const void* x, int64_t x_rows, int64_t K, int64
   q.out = static_cast<uint16_t*>(out);
   q.out_mode = 1;
   const int slots = (int)std::min<int64_t>(batch, E);
-  MOE_CUDA(ctx, moe::launch_qgemv(q, false, slots, (int)std::min<int64_t>(batch, 16), ctx->stream));
+  MOE_CUDA(ctx, moe::launch_qgemv(q, false, slots, (int)std::min<int64_t>((batch + slots - 1) / slots, 1 << 20), ctx->stream));
   return MOE_OK;
 }
 
@@ -797,8 +799,8 @@ int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_we
   ga.key_base = (uint32_t)expert_begin;
   ga.P = P;
   ga.E = El;
-  ga.seg = kGroupSeg;
-  ga.nseg = (int)std::max<int64_t>(1, (P + kGroupSeg - 1) / kGroupSeg);
+  ga.seg = moe::group_seg(P, El);
+  ga.nseg = (int)std::max<int64_t>(1, (P + ga.seg - 1) / ga.seg);
   ga.hist = ws.hist;
   ga.segbase = ws.segbase;
   ga.offsets = ws.offsets;
@@ -817,6 +819,7 @@ int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_we
   ga.tc_min_rows = plan.min_rows;
   MOE_CUDA(ctx, moe::launch_group(ga, ctx->stream));
   const int slots = (int)std::min<int64_t>(P, El);
+  const int rows_pe = (int)std::min<int64_t>((P + E - 1) / E, 1 << 20);
   moe::QgemvArgs gu = qgemv_args(wts->gate, &wts->up, I, H);
   gu.x = static_cast<const uint16_t*>(x_all);
   gu.x_mode = 1;
@@ -826,13 +829,13 @@ int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_we
   gu.active = ws.active;
   gu.n_active = ws.n_active;
   gu.out = ws.hbuf;
+  if (plan.gemv_gu) {
+    gu.max_expert_rows = plan.gemv_skip_gu;
+    MOE_CUDA(ctx, moe::launch_qgemv(gu, true, slots, rows_pe, ctx->stream));
+  }
   if (plan.tc_gu) {
     moe::TcGemmArgs ta{gu, ws.tile_start, El, plan.max_tiles, ws.status};
     MOE_CUDA(ctx, moe::launch_tc_gemm(ta, true, ctx->stream));
-  }
-  if (plan.gemv_gu) {
-    gu.max_expert_rows = plan.gemv_skip_gu;
-    MOE_CUDA(ctx, moe::launch_qgemv(gu, true, slots, 8, ctx->stream));
   }
   moe::QgemvArgs dn = qgemv_args(wts->down, nullptr, H, I);
   dn.x = ws.hbuf;
@@ -842,13 +845,13 @@ int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_we
   dn.active = ws.active;
   dn.n_active = ws.n_active;
   dn.out = ws.ybuf;
+  if (plan.gemv_dn) {
+    dn.max_expert_rows = plan.gemv_skip_dn;
+    MOE_CUDA(ctx, moe::launch_qgemv(dn, false, slots, rows_pe, ctx->stream));
+  }
   if (plan.tc_dn) {
     moe::TcGemmArgs ta{dn, ws.tile_start, El, plan.max_tiles, ws.status};
     MOE_CUDA(ctx, moe::launch_tc_gemm(ta, false, ctx->stream));
-  }
-  if (plan.gemv_dn) {
-    dn.max_expert_rows = plan.gemv_skip_dn;
-    MOE_CUDA(ctx, moe::launch_qgemv(dn, false, slots, 8, ctx->stream));
   }
   moe::EpPartialArgs pa{};
   pa.y = ws.ybuf;

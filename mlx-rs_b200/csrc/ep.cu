@@ -30,17 +30,35 @@ __global__ void __launch_bounds__(256) ep_partial_kernel(EpPartialArgs a) {
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-  for (int j = 0; j < a.k; ++j) {
-    const int64_t p = (int64_t)t * a.k + j;
-    const uint32_t pk = a.packed[p];
-    if ((pk & 0xffffu) - a.e0 >= (uint32_t)a.E_l) continue;  // another rank's expert
-    const float wj = bf2f((uint16_t)(pk >> 16));
-    const uint4 v = *reinterpret_cast<const uint4*>(a.y + (size_t)a.inv[p] * a.H + h);
-    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+  // k terms in batches of 4 with their loads in flight together, summed in index order
+  for (int j0 = 0; j0 < a.k; j0 += 4) {
+    uint4 v[4];
+    float wj[4];
+    bool loc[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      acc[2 * i] = __fadd_rn(acc[2 * i], rbf(__fmul_rn(bf_lo(u[i]), wj)));
-      acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], rbf(__fmul_rn(bf_hi(u[i]), wj)));
+    for (int jj = 0; jj < 4; ++jj) {
+      const int j = j0 + jj;
+      loc[jj] = false;
+      if (j < a.k) {
+        const int64_t p = (int64_t)t * a.k + j;
+        const uint32_t pk = a.packed[p];
+        loc[jj] = (pk & 0xffffu) - a.e0 < (uint32_t)a.E_l;  // else another rank's expert
+        if (loc[jj]) {
+          wj[jj] = bf2f((uint16_t)(pk >> 16));
+          v[jj] = *reinterpret_cast<const uint4*>(a.y + (size_t)a.inv[p] * a.H + h);
+        }
+      }
+    }
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      if (loc[jj]) {
+        const uint32_t u[4] = {v[jj].x, v[jj].y, v[jj].z, v[jj].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc[2 * i] = __fadd_rn(acc[2 * i], rbf(__fmul_rn(bf_lo(u[i]), wj[jj])));
+          acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], rbf(__fmul_rn(bf_hi(u[i]), wj[jj])));
+        }
+      }
     }
   }
   float4* dst = reinterpret_cast<float4*>(a.partial + (size_t)t * a.H + h);

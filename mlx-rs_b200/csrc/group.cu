@@ -6,14 +6,14 @@
 // bit for bit: offsets[e] = exclusive prefix sum of the counts, and within expert e
 // the pairs p = t*k + j appear in ascending p.
 //
-// Small inputs (P <= 32768, E <= 512) take one launch of one CTA (group_small_kernel):
+// Small inputs (P <= 8192, E <= 512) take one launch of one CTA (group_small_kernel):
 // 32 warps each own a contiguous segment of the pairs; per-warp histograms in shared
 // memory give every warp its per-expert base, and each warp then ranks its pairs in
 // order with __match_any_sync. Larger inputs take three launches over segments of
 // `seg` consecutive pairs:
 //   hist:    per-segment histograms (shared-memory atomics; counts are order-free);
-//   scan:    one CTA: per-expert prefix over segments, exclusive scan over experts,
-//            the ascending list of active experts;
+//   scan:    one CTA: per-expert prefix over segments (histogram staged in shared
+//            memory), exclusive scan over experts, the ascending list of active experts;
 //   scatter: one warp per segment walks its pairs in order, 32 at a time; lanes with
 //            the same expert are ranked by __match_any_sync, so positions follow p.
 #include "common.cuh"
@@ -134,23 +134,31 @@ __global__ void group_hist_kernel(GroupArgs a) {
   for (int e = threadIdx.x; e < a.E; e += blockDim.x) a.hist[(size_t)g * a.E + e] = sh[e];
 }
 
-// One CTA of 1024 threads; thread t owns experts 4t .. 4t+3 (E <= 4096).
+// One CTA of 1024 threads; thread t owns experts 4t .. 4t+3 (E <= 4096). The [nseg, E]
+// histogram is staged in shared memory (nseg * E * 4 bytes, sized by the caller's
+// choice of segment length), so the per-expert prefix over segments runs at shared
+// memory latency; the results go back to global memory coalesced.
 __global__ void __launch_bounds__(1024) group_scan_kernel(GroupArgs a) {
+  extern __shared__ int32_t hs[];  // [nseg][E]
   __shared__ int32_t warp_tot[32];
-  __shared__ int32_t warp_act[32];
+  __shared__ int32_t n_act;
   constexpr int EPT = 4;
   const int tid = threadIdx.x;
+  const int E = a.E;
+  const int n = a.nseg * E;
   pdl_wait();
+  for (int i = tid; i < n; i += 1024) hs[i] = a.hist[i];
+  __syncthreads();
   int32_t tot[EPT];
   int32_t my_sum = 0, my_act = 0;
 #pragma unroll
   for (int i = 0; i < EPT; ++i) {
     const int e = tid * EPT + i;
     int32_t run = 0;
-    if (e < a.E) {
+    if (e < E) {
       for (int g = 0; g < a.nseg; ++g) {
-        const int32_t h = a.hist[(size_t)g * a.E + e];
-        a.segbase[(size_t)g * a.E + e] = run;
+        const int32_t h = hs[g * E + e];
+        hs[g * E + e] = run;
         run += h;
       }
     }
@@ -158,64 +166,46 @@ __global__ void __launch_bounds__(1024) group_scan_kernel(GroupArgs a) {
     my_sum += run;
     my_act += run > 0 ? 1 : 0;
   }
-  // Block-wide exclusive scan of my_sum and my_act (thread order = expert order).
-  const int lane = tid & 31, warp = tid >> 5;
-  int32_t incl = my_sum, incl_a = my_act;
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const int32_t v = __shfl_up_sync(0xffffffffu, incl, off);
-    const int32_t va = __shfl_up_sync(0xffffffffu, incl_a, off);
-    if (lane >= off) {
-      incl += v;
-      incl_a += va;
-    }
-  }
-  if (lane == 31) {
-    warp_tot[warp] = incl;
-    warp_act[warp] = incl_a;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    int32_t v = warp_tot[lane], va = warp_act[lane];
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int32_t u = __shfl_up_sync(0xffffffffu, v, off);
-      const int32_t ua = __shfl_up_sync(0xffffffffu, va, off);
-      if (lane >= off) {
-        v += u;
-        va += ua;
-      }
-    }
-    warp_tot[lane] = v;
-    warp_act[lane] = va;
-  }
-  __syncthreads();
-  int32_t base = incl - my_sum + (warp > 0 ? warp_tot[warp - 1] : 0);
-  int32_t abase = incl_a - my_act + (warp > 0 ? warp_act[warp - 1] : 0);
+  const int32_t base0 = block_exclusive_scan(my_sum, warp_tot, nullptr);
+  const int32_t abase0 = block_exclusive_scan(my_act, warp_tot, &n_act);
+  int32_t base = base0, abase = abase0;
+  int32_t ebase[EPT];
 #pragma unroll
   for (int i = 0; i < EPT; ++i) {
     const int e = tid * EPT + i;
-    if (e < a.E) {
+    ebase[i] = base;
+    if (e < E) {
       a.offsets[e] = base;
-      for (int g = 0; g < a.nseg; ++g) a.segbase[(size_t)g * a.E + e] += base;
       if (tot[i] > 0) a.active[abase++] = e;
       base += tot[i];
     }
   }
-  if (tid == 0) *a.n_active = warp_act[31];
-  if (tid * EPT < a.E && (tid + 1) * EPT >= a.E) a.offsets[a.E] = base;  // total of valid pairs
+  if (tid * EPT < E && (tid + 1) * EPT >= E) a.offsets[E] = base;  // total of valid pairs
+  if (tid == 0) *a.n_active = n_act;
   if (a.tile_start) {
-    __syncthreads();
-    if (tid == 0) {
-      int32_t run = 0;
-      for (int e = 0; e < a.E; ++e) {
-        a.tile_start[e] = run;
-        const int32_t cnt = a.offsets[e + 1] - a.offsets[e];
-        if (cnt >= a.tc_min_rows) run += (cnt + a.tile_rows - 1) / a.tile_rows;
-      }
-      a.tile_start[a.E] = run;
+    int32_t nt[EPT], my_nt = 0;
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      nt[i] = (tid * EPT + i < E && tot[i] >= a.tc_min_rows) ? (tot[i] + a.tile_rows - 1) / a.tile_rows : 0;
+      my_nt += nt[i];
+    }
+    int32_t tb = block_exclusive_scan(my_nt, warp_tot, nullptr);
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      const int e = tid * EPT + i;
+      if (e <= E) a.tile_start[e] = tb;  // entry E (the total) from the thread past the last expert
+      tb += nt[i];
     }
   }
+  // segment bases in shared memory -> global, plus the expert's base
+#pragma unroll
+  for (int i = 0; i < EPT; ++i) {
+    const int e = tid * EPT + i;
+    if (e < E)
+      for (int g = 0; g < a.nseg; ++g) hs[g * E + e] += ebase[i];
+  }
+  __syncthreads();
+  for (int i = tid; i < n; i += 1024) a.segbase[i] = hs[i];
 }
 
 __global__ void group_scatter_kernel(GroupArgs a) {
@@ -253,7 +243,7 @@ cudaError_t launch_group(const GroupArgs& a, cudaStream_t st) {
     if (err != cudaSuccess) return err;
     return cudaMemsetAsync(a.n_active, 0, sizeof(int32_t), st);
   }
-  if (a.P <= 32768 && a.E <= 512) {
+  if (a.P <= 8192 && a.E <= 512) {
     const size_t smem = sizeof(int32_t) * 32 * a.E;
     static thread_local int set_dev = -1;
     int dev = 0;
@@ -267,9 +257,22 @@ cudaError_t launch_group(const GroupArgs& a, cudaStream_t st) {
     return launch_k(group_small_kernel, dim3(1), dim3(1024), smem, st, a);
   }
   const size_t sh = sizeof(int32_t) * a.E;
+  const size_t scan_sh = sizeof(int32_t) * (size_t)a.nseg * a.E;
+  if (scan_sh > kGroupScanSmem) return cudaErrorInvalidValue;  // the caller's segment length is too short
+  {
+    static thread_local int set_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev != set_dev) {
+      cudaError_t err = cudaFuncSetAttribute(group_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kGroupScanSmem);
+      if (err != cudaSuccess) return err;
+      set_dev = dev;
+    }
+  }
   cudaError_t err = launch_k(group_hist_kernel, dim3(a.nseg), dim3(256), sh, st, a);
   if (err != cudaSuccess) return err;
-  err = launch_k(group_scan_kernel, dim3(1), dim3(1024), 0, st, a);
+  err = launch_k(group_scan_kernel, dim3(1), dim3(1024), scan_sh, st, a);
   if (err != cudaSuccess) return err;
   return launch_k(group_scatter_kernel, dim3(a.nseg), dim3(32), sh, st, a);
 }

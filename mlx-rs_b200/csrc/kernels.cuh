@@ -110,12 +110,22 @@ struct CombineArgs {
   uint16_t* out;            // [T, H]
 };
 
+// Segment length of the grouping for P pairs over E experts: short segments (more
+// parallel scatter warps) while the [nseg, E] histogram fits the scan's shared memory.
+constexpr size_t kGroupScanSmem = 192 * 1024;
+inline int group_seg(int64_t P, int E) {
+  int seg = 256;
+  while ((size_t)((P + seg - 1) / seg) * (size_t)E * 4 > kGroupScanSmem) seg *= 2;
+  return seg;
+}
+
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t st);
 cudaError_t launch_topk(const TopkArgs& a, cudaStream_t st);
 cudaError_t launch_group(const GroupArgs& a, cudaStream_t st);
-// gated: out = swiglu(x.W0^T, x.W1^T); else out = x.W0^T. max_rows_per_expert bounds
-// the token chunk the kernel stages at once; slots = grid.y.
-cudaError_t launch_qgemv(const QgemvArgs& a, bool gated, int slots, int max_rows_per_expert,
+// gated: out = swiglu(x.W0^T, x.W1^T); else out = x.W0^T. rows_per_expert (the expected
+// rows of an expert) sets how many tokens one pass over the weights serves; slots = the
+// number of expert slots of the grid.
+cudaError_t launch_qgemv(const QgemvArgs& a, bool gated, int slots, int rows_per_expert,
                          cudaStream_t st);
 // Grouped GEMM on tcgen05 tensor cores for the prefill regime (many rows per expert):
 // one CTA = 128 weight rows x up to 256 rows (tokens) of one expert. Requires N % 128 == 0

@@ -18,7 +18,9 @@
 //   * after the last stage the producer warps read the accumulators back with
 //     tcgen05.ld (warp w owns TMEM lanes 32(w%4).. = weight rows, and every other block
 //     of 32 token columns by w/4); in the gated form the gate and up accumulators (TMEM
-//     columns 0 and 256) are combined by SwiGLU in registers. Each warp transposes its
+//     columns 0 and 256) are combined by SwiGLU in registers (bf16 multiplies exact as in
+//     the reference; the sigmoid from the hardware ex2/rcp approximations, which is why
+//     this path has its own tolerance against the oracle). Each warp transposes its
 //     32 x 32 tile through shared memory so that the outputs leave as 16-byte stores.
 // The shared-memory ring has kStages stages guarded by full/empty mbarriers. Every
 // mbarrier wait is bounded; on expiry the CTA records a status code and drains out.
@@ -176,6 +178,36 @@ MOE_DEV uint4 lds_v4(uint32_t a) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
   return v;
+}
+
+// Two fp32 values -> packed bf16 pair (lo = a), round to nearest even (cvt.rn.bf16x2).
+MOE_DEV uint32_t pack_bf2(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;\n" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
+MOE_DEV uint32_t bf2_mul(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+// sigmoid(x) from the hardware base-2 exponential and reciprocal approximations
+// (relative error a few fp32 ulps; the result is rounded to bf16 by the caller).
+MOE_DEV float sigmoid_fast(float x) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(e) : "f"(x * -1.4426950408889634f));
+  asm("rcp.approx.ftz.f32 %0, %1;\n" : "=f"(r) : "f"(1.0f + e));
+  return r;
+}
+// SwiGLU of two (gate, up) pairs on the tensor-core path: h = bf16(bf16(g * bf16(sig(g))) * u)
+// with g and u first rounded to bf16 (the bf16 outputs of the two projections). The
+// products of bf16 values are exact in fp32, so mul.rn.bf16x2 rounds them as the
+// reference's bf16 multiplies do; only sigmoid is approximate (see sigmoid_fast).
+MOE_DEV uint32_t swiglu2_fast(float g0, float g1, float u0, float u1) {
+  const uint32_t g2 = pack_bf2(g0, g1), u2 = pack_bf2(u0, u1);
+  const float gr0 = bf_lo(g2), gr1 = bf_hi(g2);
+  const uint32_t s2 = pack_bf2(sigmoid_fast(gr0), sigmoid_fast(gr1));
+  return bf2_mul(bf2_mul(g2, s2), u2);
 }
 
 // Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled K-major tile.
@@ -380,14 +412,19 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
           uint32_t u[32];
           tmem_ld32(tl + 256 + c0, u);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const uint16_t v = swiglu_bf16(rbf(__uint_as_float(g[j])), rbf(__uint_as_float(u[j])));
-            *reinterpret_cast<uint16_t*>(tile + j * 64 + lane * 2) = v;
+          for (int j = 0; j < 32; j += 2) {
+            const uint32_t h2 = swiglu2_fast(__uint_as_float(g[j]), __uint_as_float(g[j + 1]),
+                                             __uint_as_float(u[j]), __uint_as_float(u[j + 1]));
+            *reinterpret_cast<uint16_t*>(tile + j * 64 + lane * 2) = (uint16_t)(h2 & 0xffffu);
+            *reinterpret_cast<uint16_t*>(tile + (j + 1) * 64 + lane * 2) = (uint16_t)(h2 >> 16);
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            *reinterpret_cast<uint16_t*>(tile + j * 64 + lane * 2) = f2bf(__uint_as_float(g[j]));
+          for (int j = 0; j < 32; j += 2) {
+            const uint32_t o2 = pack_bf2(__uint_as_float(g[j]), __uint_as_float(g[j + 1]));
+            *reinterpret_cast<uint16_t*>(tile + j * 64 + lane * 2) = (uint16_t)(o2 & 0xffffu);
+            *reinterpret_cast<uint16_t*>(tile + (j + 1) * 64 + lane * 2) = (uint16_t)(o2 >> 16);
+          }
         }
         __syncwarp();
         // token row t of the tile = 64 bytes = 4 x 16 bytes; lane -> (t = lane/4 + 8i, piece lane%4)

@@ -110,10 +110,11 @@ struct RowMap {
 //   rings [warps][kStages][MT*16 rows][128 B]  weight chunks; the 32-byte group slot of
 //         ring row r is stored at slot (group ^ (r & 3)), which keeps the lanes' 8-byte
 //         fragment reads conflict-free.
-template <bool GATED, int MT>
+template <bool GATED, int MT, int NC>
 __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_expert, int ctas_per_expert,
                                                     int max_slots) {
   constexpr int ROWS = GATED ? 8 * MT : 16 * MT;  // output rows per unit
+  constexpr int TOK = kTok * NC;                  // tokens per pass over the weights
   constexpr int kRingRows = MT * 16;
   constexpr int kStageBytes = kRingRows * kKC * 32;
   constexpr int kPieces = kRingRows * kKC * 2 / 32;  // 16-byte copies per lane per chunk
@@ -138,9 +139,9 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
   const int xrow_bytes = 2 * K + 16;
   const uint32_t smem_s = (uint32_t)__cvta_generic_to_shared(smem);
   const uint32_t xperm_s = smem_s;
-  const uint32_t xsum_s = xperm_s + kTok * xrow_bytes;
-  float* xsum = reinterpret_cast<float*>(smem + kTok * xrow_bytes);
-  const uint32_t ring_s = xsum_s + G * kTok * 4 + warp * kStages * kStageBytes;
+  const uint32_t xsum_s = xperm_s + TOK * xrow_bytes;
+  float* xsum = reinterpret_cast<float*>(smem + TOK * xrow_bytes);
+  const uint32_t ring_s = xsum_s + G * TOK * 4 + warp * kStages * kStageBytes;
 
   // ring row -> global weight row (clamped into the matrix: rows past N compute junk
   // that is never stored)
@@ -222,8 +223,8 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
                                (GATED ? (reinterpret_cast<uintptr_t>(a.s1) | reinterpret_cast<uintptr_t>(a.b1)) : 0);
   const bool vec_scales = (G & 3) == 0 && (align_bits & 7) == 0;
 
-  for (int64_t cbase = row_begin; cbase < row_end; cbase += kTok) {
-    const int ntok = (row_end - cbase < kTok) ? (int)(row_end - cbase) : kTok;
+  for (int64_t cbase = row_begin; cbase < row_end; cbase += TOK) {
+    const int ntok = (row_end - cbase < TOK) ? (int)(row_end - cbase) : TOK;
     reset_src();
     if (unit_live) issue_chunk(0);
     __syncthreads();  // the previous chunk's readers of xperm/xsum are done
@@ -263,21 +264,23 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
         uint4* d = reinterpret_cast<uint4*>(smem + (size_t)t * xrow_bytes + g * 128 + c * 32);
         d[0] = o0;
         d[1] = o1;
-        if (c == 0) xsum[g * kTok + t] = ps;
+        if (c == 0) xsum[g * TOK + t] = ps;
       }
     }
     // tokens past ntok: zero sums (their MMA columns are never stored; zeros keep them finite)
-    for (int i = tid; i < G * kTok; i += blockDim.x)
-      if ((i % kTok) >= ntok) xsum[i] = 0.0f;
+    for (int i = tid; i < G * TOK; i += blockDim.x)
+      if ((i % TOK) >= ntok) xsum[i] = 0.0f;
     __syncthreads();
     if (!unit_live) continue;
 
-    const uint32_t xb = xperm_s + gq * xrow_bytes + cq * 32;  // token gq's fragment base
-    float acc[MT][4];
+    const uint32_t xb = xperm_s + gq * xrow_bytes + cq * 32;  // token gq's fragment base (chunk 0)
+    float acc[NC][MT][4];
 #pragma unroll
-    for (int t = 0; t < MT; ++t)
+    for (int n = 0; n < NC; ++n)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) acc[t][q] = 0.0f;
+      for (int t = 0; t < MT; ++t)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[n][t][q] = 0.0f;
 
     // scales of the lane's rows, (s, b) for kKC groups, loaded one chunk ahead
     uint32_t sw[MT][2][2], bw[MT][2][2];  // [tile][lo/hi][pair of groups]
@@ -319,22 +322,32 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
       for (int gl = 0; gl < kKC; ++gl) {
         const int g = g0 + gl;
         if (g < G) {
-          const uint4 v0 = lds_u4(xb + g * 128), v1 = lds_u4(xb + g * 128 + 16);
-          const uint32_t bfr[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-          const float2 X = lds_f2(xsum_s + (g * kTok + 2 * cq) * 4);  // tokens 2cq, 2cq+1
+          uint32_t bfr[NC][8];
+          float2 X[NC];
+#pragma unroll
+          for (int n = 0; n < NC; ++n) {
+            const uint32_t xbn = xb + n * kTok * xrow_bytes;
+            const uint4 v0 = lds_u4(xbn + g * 128), v1 = lds_u4(xbn + g * 128 + 16);
+            bfr[n][0] = v0.x; bfr[n][1] = v0.y; bfr[n][2] = v0.z; bfr[n][3] = v0.w;
+            bfr[n][4] = v1.x; bfr[n][5] = v1.y; bfr[n][6] = v1.z; bfr[n][7] = v1.w;
+            X[n] = lds_f2(xsum_s + (g * TOK + n * kTok + 2 * cq) * 4);  // tokens 2cq, 2cq+1 of chunk n
+          }
 #pragma unroll
           for (int t = 0; t < MT; ++t) {
             const int rr = t * 16 + gq;
             const uint32_t off = ((gl ^ (rr & 3)) * 32) + cq * 8;
             const uint2 wlo = lds_u2(st + rr * (kKC * 32) + off);
             const uint2 whi = lds_u2(st + (rr + 8) * (kKC * 32) + off);
-            float d[4];
+            float d[NC][4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const uint32_t a0 = nib_pair(wlo.x, j), a1 = nib_pair(whi.x, j);
               const uint32_t a2 = nib_pair(wlo.y, j), a3 = nib_pair(whi.y, j);
-              if (j == 0) mma_first(d, a0, a1, a2, a3, bfr[0], bfr[1]);
-              else mma_acc(d, a0, a1, a2, a3, bfr[2 * j], bfr[2 * j + 1]);
+#pragma unroll
+              for (int n = 0; n < NC; ++n) {
+                if (j == 0) mma_first(d[n], a0, a1, a2, a3, bfr[n][0], bfr[n][1]);
+                else mma_acc(d[n], a0, a1, a2, a3, bfr[n][2 * j], bfr[n][2 * j + 1]);
+              }
             }
             const uint32_t s_lo2 = sw[t][0][gl >> 1], s_hi2 = sw[t][1][gl >> 1];
             const uint32_t b_lo2 = bw[t][0][gl >> 1], b_hi2 = bw[t][1][gl >> 1];
@@ -342,10 +355,13 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
             const float s_h = (gl & 1) ? bf_hi(s_hi2) : bf_lo(s_hi2);
             const float c_l = __fmaf_rn(-128.0f, s_l, (gl & 1) ? bf_hi(b_lo2) : bf_lo(b_lo2));
             const float c_h = __fmaf_rn(-128.0f, s_h, (gl & 1) ? bf_hi(b_hi2) : bf_lo(b_hi2));
-            acc[t][0] = __fmaf_rn(c_l, X.x, __fmaf_rn(s_l, d[0], acc[t][0]));
-            acc[t][1] = __fmaf_rn(c_l, X.y, __fmaf_rn(s_l, d[1], acc[t][1]));
-            acc[t][2] = __fmaf_rn(c_h, X.x, __fmaf_rn(s_h, d[2], acc[t][2]));
-            acc[t][3] = __fmaf_rn(c_h, X.y, __fmaf_rn(s_h, d[3], acc[t][3]));
+#pragma unroll
+            for (int n = 0; n < NC; ++n) {
+              acc[n][t][0] = __fmaf_rn(c_l, X[n].x, __fmaf_rn(s_l, d[n][0], acc[n][t][0]));
+              acc[n][t][1] = __fmaf_rn(c_l, X[n].y, __fmaf_rn(s_l, d[n][1], acc[n][t][1]));
+              acc[n][t][2] = __fmaf_rn(c_h, X[n].x, __fmaf_rn(s_h, d[n][2], acc[n][t][2]));
+              acc[n][t][3] = __fmaf_rn(c_h, X[n].y, __fmaf_rn(s_h, d[n][3], acc[n][t][3]));
+            }
           }
         }
       }
@@ -365,31 +381,33 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
     cp_wait<0>();
     pdl_trigger();
 
-    // ---- epilogue: C fragment (MMA rows gq / gq+8, tokens 2cq / 2cq+1)
+    // ---- epilogue: C fragment (MMA rows gq / gq+8, tokens 2cq / 2cq+1 of each chunk)
 #pragma unroll
-    for (int cc = 0; cc < 2; ++cc) {
-      const int tok = 2 * cq + cc;
-      if (tok < ntok) {
-        const int64_t pos = cbase + tok;
-        const int64_t orow = a.out_mode == 0 ? pos : rm.orig(pos);
-        uint16_t* o = a.out + (size_t)orow * N;
+    for (int n = 0; n < NC; ++n)
 #pragma unroll
-        for (int t = 0; t < MT; ++t) {
-          if (GATED) {
-            const int row = r0 + 8 * t + gq;
-            if (row < N) o[row] = swiglu_bf16(rbf(acc[t][cc]), rbf(acc[t][2 + cc]));
-          } else {
-            const int row = r0 + 16 * t + gq;
-            if (row < N) o[row] = f2bf(acc[t][cc]);
-            if (row + 8 < N) o[row + 8] = f2bf(acc[t][2 + cc]);
+      for (int cc = 0; cc < 2; ++cc) {
+        const int tok = n * kTok + 2 * cq + cc;
+        if (tok < ntok) {
+          const int64_t pos = cbase + tok;
+          const int64_t orow = a.out_mode == 0 ? pos : rm.orig(pos);
+          uint16_t* o = a.out + (size_t)orow * N;
+#pragma unroll
+          for (int t = 0; t < MT; ++t) {
+            if (GATED) {
+              const int row = r0 + 8 * t + gq;
+              if (row < N) o[row] = swiglu_bf16(rbf(acc[n][t][cc]), rbf(acc[n][t][2 + cc]));
+            } else {
+              const int row = r0 + 16 * t + gq;
+              if (row < N) o[row] = f2bf(acc[n][t][cc]);
+              if (row + 8 < N) o[row + 8] = f2bf(acc[n][t][2 + cc]);
+            }
           }
         }
       }
-    }
   }
 }
 
-template <bool GATED, int MT>
+template <bool GATED, int MT, int NC>
 static cudaError_t launch_qgemv_t(const QgemvArgs& a, int slots, int wpc, cudaStream_t st) {
   constexpr int ROWS = GATED ? 8 * MT : 16 * MT;
   const int upe = (a.N + ROWS - 1) / ROWS;
@@ -397,10 +415,10 @@ static cudaError_t launch_qgemv_t(const QgemvArgs& a, int slots, int wpc, cudaSt
   const long long blocks = (long long)cpe * slots;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   const int G = a.K / 64;
-  const size_t smem = (size_t)kTok * (2 * a.K + 16) + (size_t)G * kTok * 4 +
+  const size_t smem = (size_t)kTok * NC * (2 * a.K + 16) + (size_t)G * kTok * NC * 4 +
                       (size_t)wpc * kStages * MT * 16 * kKC * 32;
   if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
-  auto kern = qgemv_kernel<GATED, MT>;
+  auto kern = qgemv_kernel<GATED, MT, NC>;
   static thread_local int set_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -412,17 +430,30 @@ static cudaError_t launch_qgemv_t(const QgemvArgs& a, int slots, int wpc, cudaSt
   return launch_k(kern, dim3((unsigned)blocks), dim3(wpc * 32), smem, st, a, upe, cpe, slots);
 }
 
-cudaError_t launch_qgemv(const QgemvArgs& a, bool gated, int slots, int max_rows_per_expert,
+template <bool GATED, int NC>
+static cudaError_t launch_qgemv_nc(const QgemvArgs& a, int slots, bool wide, cudaStream_t st) {
+  return wide ? launch_qgemv_t<GATED, 2, NC>(a, slots, 8, st) : launch_qgemv_t<GATED, 1, NC>(a, slots, 4, st);
+}
+
+cudaError_t launch_qgemv(const QgemvArgs& a, bool gated, int slots, int rows_per_expert,
                          cudaStream_t st) {
-  (void)max_rows_per_expert;  // tokens are processed in chunks of 8
   if (slots <= 0) return cudaSuccess;
   // Wide units (two m16 tiles per warp) and 8-warp CTAs when there is enough work to
   // fill the GPU; narrow units in 4-warp CTAs otherwise, for parallelism.
   const int rows2 = gated ? 16 : 32;
   const bool wide = (long long)slots * ((a.N + rows2 - 1) / rows2) >= 148 * 16;
-  const int wpc = wide ? 8 : 4;
-  if (gated) return wide ? launch_qgemv_t<true, 2>(a, slots, wpc, st) : launch_qgemv_t<true, 1>(a, slots, wpc, st);
-  return wide ? launch_qgemv_t<false, 2>(a, slots, wpc, st) : launch_qgemv_t<false, 1>(a, slots, wpc, st);
+  // Tokens per pass over an expert's weights: 8, 16 or 32 by the expected rows per
+  // expert (an expert with more rows takes more passes), while the staged rows fit.
+  int nc = rows_per_expert > 16 ? 4 : rows_per_expert > 8 ? 2 : 1;
+  while (nc > 1 && (size_t)kTok * nc * (2 * a.K + 16) > 140 * 1024) nc >>= 1;
+  if (gated) {
+    if (nc == 4) return launch_qgemv_nc<true, 4>(a, slots, wide, st);
+    if (nc == 2) return launch_qgemv_nc<true, 2>(a, slots, wide, st);
+    return launch_qgemv_nc<true, 1>(a, slots, wide, st);
+  }
+  if (nc == 4) return launch_qgemv_nc<false, 4>(a, slots, wide, st);
+  if (nc == 2) return launch_qgemv_nc<false, 2>(a, slots, wide, st);
+  return launch_qgemv_nc<false, 1>(a, slots, wide, st);
 }
 
 }  // namespace moe

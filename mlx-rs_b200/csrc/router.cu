@@ -18,7 +18,7 @@
 namespace moe {
 
 template <int NE, int NT>
-__global__ void __launch_bounds__(128) router_logits_kernel(RouterArgs a) {
+__global__ void __launch_bounds__(128, 4) router_logits_kernel(RouterArgs a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int row0 = (blockIdx.x * 4 + warp) * NE;
   const int t0 = blockIdx.y * NT;
@@ -52,22 +52,19 @@ __global__ void __launch_bounds__(128) router_logits_kernel(RouterArgs a) {
 
   for (int c = lane; c < nchunks; c += 32) {
     const int g = (c * 32) / a.group_size;
-    uint4 wv[NE];
     float sc[NE], bi[NE];
 #pragma unroll
     for (int e = 0; e < NE; ++e) {
-      if (rvalid[e]) {
-        wv[e] = __ldg(reinterpret_cast<const uint4*>(wrow[e] + (size_t)c * 4));
-        sc[e] = bf2f(__ldg(srow[e] + g));
-        bi[e] = brow[e] ? bf2f(__ldg(brow[e] + g)) : 0.0f;
-      } else {
-        wv[e] = make_uint4(0, 0, 0, 0);
-        sc[e] = 0.0f;
-        bi[e] = 0.0f;
-      }
+      sc[e] = rvalid[e] ? bf2f(__ldg(srow[e] + g)) : 0.0f;
+      bi[e] = (rvalid[e] && brow[e]) ? bf2f(__ldg(brow[e] + g)) : 0.0f;
     }
-#pragma unroll
+    // one 8-element word at a time (not unrolled: keeps the token rows of a single word
+    // in registers, so that more warps fit on an SM to hide the load latency)
+#pragma unroll 1
     for (int word = 0; word < 4; ++word) {
+      uint32_t wv[NE];
+#pragma unroll
+      for (int e = 0; e < NE; ++e) wv[e] = rvalid[e] ? __ldg(wrow[e] + (size_t)c * 4 + word) : 0u;
       uint4 xv[NT];
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
@@ -80,8 +77,9 @@ __global__ void __launch_bounds__(128) router_logits_kernel(RouterArgs a) {
         float wq[NE];
 #pragma unroll
         for (int e = 0; e < NE; ++e) {
-          const uint32_t wd = word == 0 ? wv[e].x : word == 1 ? wv[e].y : word == 2 ? wv[e].z : wv[e].w;
-          const float q = (float)((wd >> (4 * el)) & 0xfu);
+          const uint32_t wd = wv[e];
+          // q as an exact float: the field in the mantissa of 2^23, minus 2^23
+          const float q = __fsub_rn(__uint_as_float(((wd >> (4 * el)) & 0xfu) | 0x4b000000u), 8388608.0f);
           wq[e] = __fmaf_rn(sc[e], q, bi[e]);
         }
 #pragma unroll
