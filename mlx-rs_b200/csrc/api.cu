@@ -287,6 +287,20 @@ enum Stage { kRouter = 0, kTopk, kGroup, kGateUp, kDown, kSharedGateUp, kSharedD
     if (ev) MOE_CUDA(ctx, cudaEventRecord((ev)[i], st)); \
   } while (0)
 
+// The status block (first 256 bytes of the scratch, zeroed when allocated): word 0 is
+// the device status (bounded waits that expired); words from kFusedCounterWord are the
+// ticket counters of the fused routing kernel, which leaves them zero.
+constexpr int kFusedCounterWord = 32;
+static_assert(kFusedCounterWord + moe::kFusedRouteCounters <= 64, "status block");
+
+// Opt-in (MOE_B200_FUSED_ROUTE=1): on the B200 the three launches chained by
+// programmatic dependent launch finish sooner at decode sizes than the fused kernel,
+// whose top-k and grouping run on the last CTAs only.
+bool fused_route_enabled() {
+  const char* v = std::getenv("MOE_B200_FUSED_ROUTE");
+  return v && v[0] == '1';
+}
+
 // Routing + grouping of one block call into ws.
 // With `packed`, routing writes [T, k] expert | bf16(weight) << 16 there and stops
 // before the grouping (the expert-parallel route).
@@ -309,7 +323,6 @@ int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* 
   ra.gate_b = static_cast<const uint16_t*>(w->shared_expert_gate.biases);
   ra.logits = ws.logits;
   MOE_MARK(ev, kRouter, ctx->stream);
-  MOE_CUDA(ctx, moe::launch_router(ra, ctx->stream));
 
   moe::TopkArgs ta{};
   ta.logits = ws.logits;
@@ -324,9 +337,6 @@ int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* 
   ta.weights = packed ? nullptr : ws.wsel;
   ta.packed = packed;
   ta.gate_val = gate_row ? ws.gate_val : nullptr;
-  MOE_MARK(ev, kTopk, ctx->stream);
-  MOE_CUDA(ctx, moe::launch_topk(ta, ctx->stream));
-  if (packed) return MOE_OK;
 
   moe::GroupArgs ga{};
   ga.key = ws.idx;
@@ -344,6 +354,20 @@ int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* 
   ga.tile_start = ws.tile_start;
   ga.tile_rows = moe::kTcTileRows;
   ga.tc_min_rows = tc_min_rows;
+
+  // Decode-sized batches, when enabled: one launch (router, top-k and grouping; the
+  // stage split of moe_block_profile then books all of it as "router").
+  if (moe::route_fused_fits((int)T, E, ga.P) && fused_route_enabled()) {
+    MOE_CUDA(ctx, moe::launch_route_fused(ra, ta, packed ? nullptr : &ga,
+                                          reinterpret_cast<uint32_t*>(ws.status) + kFusedCounterWord, ctx->stream));
+    MOE_MARK(ev, kTopk, ctx->stream);
+    MOE_MARK(ev, kGroup, ctx->stream);
+    return MOE_OK;
+  }
+  MOE_CUDA(ctx, moe::launch_router(ra, ctx->stream));
+  MOE_MARK(ev, kTopk, ctx->stream);
+  MOE_CUDA(ctx, moe::launch_topk(ta, ctx->stream));
+  if (packed) return MOE_OK;
   MOE_MARK(ev, kGroup, ctx->stream);
   MOE_CUDA(ctx, moe::launch_group(ga, ctx->stream));
   return MOE_OK;

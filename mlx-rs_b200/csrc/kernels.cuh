@@ -120,6 +120,13 @@ inline int group_seg(int64_t P, int E) {
 }
 
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t st);
+// Router + top-k (+ grouping when ga is non-null) in one launch for T <= 64 tokens
+// (route_fused_fits). counters: kFusedRouteCounters zero-initialised words, left zero.
+constexpr int kFusedRouteMaxTokens = 64;
+constexpr int kFusedRouteCounters = kFusedRouteMaxTokens / 4 + 1;
+bool route_fused_fits(int T, int E, int64_t P);
+cudaError_t launch_route_fused(const RouterArgs& ra, const TopkArgs& ta, const GroupArgs* ga, uint32_t* counters,
+                               cudaStream_t st);
 cudaError_t launch_topk(const TopkArgs& a, cudaStream_t st);
 cudaError_t launch_group(const GroupArgs& a, cudaStream_t st);
 // gated: out = swiglu(x.W0^T, x.W1^T); else out = x.W0^T. rows_per_expert (the expected

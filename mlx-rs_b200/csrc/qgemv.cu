@@ -9,7 +9,9 @@
 // token rows are staged once per CTA: read from global memory, permuted into the MMA
 // fragment order and stored in shared memory together with their per-group sums.
 // Each warp streams its weight rows through its own shared-memory ring with coalesced
-// 16-byte cp.async copies (a row's 4 groups = 128 contiguous bytes), kStages chunks deep.
+// 16-byte cp.async copies (a row's 4 groups = 128 contiguous bytes), NS chunks deep
+// (2 for the wide units; 4 for the narrow units of small batches, where fewer warps
+// share an SM and each needs more bytes in flight).
 //
 // Arithmetic: the int4 fields become bf16 pairs holding 128 + q with one LOP3 per pair
 // (exact) and feed mma.sync.m16n8k16 with the weight rows as the M side and tokens as
@@ -36,7 +38,6 @@ namespace moe {
 namespace {
 
 constexpr int kKC = 4;      // groups per ring chunk (128 bytes of a weight row)
-constexpr int kStages = 2;  // ring depth (chunks)
 constexpr int kTok = 8;     // tokens per chunk (the MMA N)
 
 MOE_DEV void mma_acc(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -107,10 +108,10 @@ struct RowMap {
 // Shared memory:
 //   xperm [kTok][(K + 8) bf16]   staged token rows in fragment order (16-byte row pad)
 //   xsum  [G][kTok] fp32         per-token sums of each group of 64
-//   rings [warps][kStages][MT*16 rows][128 B]  weight chunks; the 32-byte group slot of
+//   rings [warps][NS][MT*16 rows][128 B]  weight chunks; the 32-byte group slot of
 //         ring row r is stored at slot (group ^ (r & 3)), which keeps the lanes' 8-byte
 //         fragment reads conflict-free.
-template <bool GATED, int MT, int NC>
+template <bool GATED, int MT, int NC, int NS>
 __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_expert, int ctas_per_expert,
                                                     int max_slots) {
   constexpr int ROWS = GATED ? 8 * MT : 16 * MT;  // output rows per unit
@@ -141,7 +142,7 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
   const uint32_t xperm_s = smem_s;
   const uint32_t xsum_s = xperm_s + TOK * xrow_bytes;
   float* xsum = reinterpret_cast<float*>(smem + TOK * xrow_bytes);
-  const uint32_t ring_s = xsum_s + G * TOK * 4 + warp * kStages * kStageBytes;
+  const uint32_t ring_s = xsum_s + G * TOK * 4 + warp * NS * kStageBytes;
 
   // ring row -> global weight row (clamped into the matrix: rows past N compute junk
   // that is never stored)
@@ -181,7 +182,7 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
     issued = 0;
   };
   auto issue_chunk = [&](int c) {
-    const uint32_t st = ring_s + (uint32_t)((c % kStages) * kStageBytes);
+    const uint32_t st = ring_s + (uint32_t)((c % NS) * kStageBytes);
     if (c + 1 < nchunks || tail_groups == kKC) {
 #pragma unroll
       for (int i = 0; i < kPieces; ++i) cp_async16(st + dst[i], src[i]);
@@ -226,7 +227,13 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
   for (int64_t cbase = row_begin; cbase < row_end; cbase += TOK) {
     const int ntok = (row_end - cbase < TOK) ? (int)(row_end - cbase) : TOK;
     reset_src();
-    if (unit_live) issue_chunk(0);
+    if (unit_live) {
+#pragma unroll
+      for (int i = 0; i < NS - 1; ++i) {
+        if (i < nchunks) issue_chunk(i);
+        else cp_commit();
+      }
+    }
     __syncthreads();  // the previous chunk's readers of xperm/xsum are done
     // ---- stage the token rows: fragment-order permutation + per-group sums
     const int units = ntok * G * 4;
@@ -310,14 +317,14 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
     };
     load_scales(0, sw, bw);
     for (int c = 0; c < nchunks; ++c) {
-      if (c + 1 < nchunks) issue_chunk(c + 1);
+      if (c + NS - 1 < nchunks) issue_chunk(c + NS - 1);
       else cp_commit();
       uint32_t swn[MT][2][2], bwn[MT][2][2];
       if (c + 1 < nchunks) load_scales(c + 1, swn, bwn);
       const int g0 = c * kKC;
-      cp_wait<1>();
+      cp_wait<NS - 1>();
       __syncwarp();
-      const uint32_t st = ring_s + (uint32_t)((c % kStages) * kStageBytes);
+      const uint32_t st = ring_s + (uint32_t)((c % NS) * kStageBytes);
 #pragma unroll
       for (int gl = 0; gl < kKC; ++gl) {
         const int g = g0 + gl;
@@ -407,7 +414,7 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
   }
 }
 
-template <bool GATED, int MT, int NC>
+template <bool GATED, int MT, int NC, int NS>
 static cudaError_t launch_qgemv_t(const QgemvArgs& a, int slots, int wpc, cudaStream_t st) {
   constexpr int ROWS = GATED ? 8 * MT : 16 * MT;
   const int upe = (a.N + ROWS - 1) / ROWS;
@@ -416,9 +423,9 @@ static cudaError_t launch_qgemv_t(const QgemvArgs& a, int slots, int wpc, cudaSt
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   const int G = a.K / 64;
   const size_t smem = (size_t)kTok * NC * (2 * a.K + 16) + (size_t)G * kTok * NC * 4 +
-                      (size_t)wpc * kStages * MT * 16 * kKC * 32;
+                      (size_t)wpc * NS * MT * 16 * kKC * 32;
   if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
-  auto kern = qgemv_kernel<GATED, MT, NC>;
+  auto kern = qgemv_kernel<GATED, MT, NC, NS>;
   static thread_local int set_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -432,7 +439,7 @@ static cudaError_t launch_qgemv_t(const QgemvArgs& a, int slots, int wpc, cudaSt
 
 template <bool GATED, int NC>
 static cudaError_t launch_qgemv_nc(const QgemvArgs& a, int slots, bool wide, cudaStream_t st) {
-  return wide ? launch_qgemv_t<GATED, 2, NC>(a, slots, 8, st) : launch_qgemv_t<GATED, 1, NC>(a, slots, 4, st);
+  return wide ? launch_qgemv_t<GATED, 2, NC, 2>(a, slots, 8, st) : launch_qgemv_t<GATED, 1, NC, 4>(a, slots, 4, st);
 }
 
 cudaError_t launch_qgemv(const QgemvArgs& a, bool gated, int slots, int rows_per_expert,

@@ -271,3 +271,27 @@ def test_tc_and_gemv_paths_agree(monkeypatch):
     for u, v in zip(a[1:], b[1:]):
         assert np.array_equal(u, v)
     assert_close(a[0].reshape(200, -1), b[0].reshape(200, -1), "tc vs gemv", ULP_TOL_TC)
+
+
+# ----------------------------------------------------------------------------------
+# fused routing (router + top-k + grouping in one launch, decode-sized batches)
+# ----------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("cfg_name,seed", [("QWEN3_30B_A3B", 1), ("QWEN15_MOE_A27B", 0), ("LFM2_8B_A1B", 3)])
+def test_fused_routing_matches_three_launches(cfg_name, seed, monkeypatch):
+    """Decode-sized batches route through one fused launch whose last CTAs run top-k and
+    the grouping; its results equal the three-launch path bit for bit, on repeated calls
+    (the ticket counters return to zero) and for every batch size up to the limit."""
+    from gpu_util import run_block
+    cfg = getattr(S, cfg_name)
+    _, blk = _block(cfg, seed)
+    for T in (1, 3, 4, 5, 17, 63, 64):
+        x = S.host_x(500 + T, T, cfg.hidden)
+        monkeypatch.setenv("MOE_B200_FUSED_ROUTE", "0")
+        ref = run_block(blk, x)
+        monkeypatch.setenv("MOE_B200_FUSED_ROUTE", "1")
+        for _ in range(2):
+            got = run_block(blk, x)
+            for u, v in zip(got[1:], ref[1:]):
+                assert np.array_equal(u, v), (cfg_name, T)
+            assert np.array_equal(got[0], ref[0]), (cfg_name, T)
