@@ -128,8 +128,21 @@ struct BlockWs {
   uint16_t* ys;
   int32_t* tile_start;
   int32_t* status;
+  float* gemv_partial;  // split-K partials of small GEMVs (null when T is large)
+  size_t gemv_partial_bytes;
   size_t bytes;
 };
+
+// Split-K partial buffer of a block call: up to 8 splits of the routed projections
+// (P <= 256 pairs) and of the shared expert (T <= 64 tokens); 0 when neither applies.
+size_t gemv_partial_floats(const moe_block_config* c, int64_t T) {
+  const int64_t P = T * c->top_k;
+  size_t n = 0;
+  if (P <= 256) n = std::max<size_t>(n, (size_t)8 * P * std::max(2 * c->moe_inter, c->hidden));
+  if (c->shared_inter > 0 && T <= 64)
+    n = std::max<size_t>(n, (size_t)8 * T * std::max(2 * c->shared_inter, c->hidden));
+  return n;
+}
 
 BlockWs carve_block(void* base, const moe_block_config* c, int64_t T) {
   Carve cv(base);
@@ -155,6 +168,9 @@ BlockWs carve_block(void* base, const moe_block_config* c, int64_t T) {
     w.hs = cv.take<uint16_t>(T * c->shared_inter);
     w.ys = cv.take<uint16_t>(T * c->hidden);
   }
+  const size_t npart = gemv_partial_floats(c, T);
+  w.gemv_partial = npart ? cv.take<float>(npart) : nullptr;
+  w.gemv_partial_bytes = npart * sizeof(float);
   w.bytes = cv.off + 256;
   return w;
 }
@@ -256,6 +272,8 @@ struct EpWs {
   int32_t *hist, *segbase, *offsets, *active, *n_active, *tile_start;
   uint32_t *perm, *inv;
   uint16_t *hbuf, *ybuf;
+  float* gemv_partial;
+  size_t gemv_partial_bytes;
   size_t bytes;
 };
 
@@ -275,6 +293,9 @@ EpWs carve_ep(void* base, const moe_block_config* c, int64_t T, int El) {
   w.inv = cv.take<uint32_t>(P);
   w.hbuf = cv.take<uint16_t>(P * c->moe_inter);
   w.ybuf = cv.take<uint16_t>(P * c->hidden);
+  const size_t npart = P <= 256 ? (size_t)8 * P * std::max(2 * c->moe_inter, c->hidden) : 0;
+  w.gemv_partial = npart ? cv.take<float>(npart) : nullptr;
+  w.gemv_partial_bytes = npart * sizeof(float);
   w.bytes = cv.off + 256;
   return w;
 }
@@ -384,9 +405,12 @@ bool use_tc(int64_t rows, int64_t experts, int N, int K) {
 }
 
 // Routed experts: each expert takes the path its own row count calls for, decided on
-// the device. Experts with at least kTcMinRows rows run on the tcgen05 GEMM (the
-// grouping gives only them tiles); the others on the GEMV, which skips the large ones.
-// MOE_B200_TC=0 puts every expert on the GEMV, =1 every expert on tcgen05.
+// the device. Experts with at least min_rows rows run on the tcgen05 GEMM (the grouping
+// gives only them tiles); the others on the GEMV, which skips the large ones. The GEMV
+// serves 8, 16 or 32 tokens per pass over an expert's weights (by the average rows per
+// expert); an expert that would need more than three passes goes to tcgen05, whose
+// dequantisation into shared memory costs about three GEMV passes. MOE_B200_TC=0 puts
+// every expert on the GEMV, =1 every expert on tcgen05.
 constexpr int kTcMinRows = 32;
 struct ExpertPlan {
   bool tc_gu = false, tc_dn = false;      // launch the tcgen05 kernel
@@ -413,11 +437,14 @@ ExpertPlan plan_experts(int64_t P, int E, int I, int H) {
     p.gemv_gu = !shape_gu;
     p.gemv_dn = !shape_dn;
   } else if (P >= kTcMinRows) {
+    const int64_t avg = (P + E - 1) / E;
+    const int pass = 8 * (avg > 16 ? 4 : avg > 8 ? 2 : 1);  // tokens per GEMV pass
+    const int thr = std::max(kTcMinRows, 3 * pass);
     p.tc_gu = shape_gu;
     p.tc_dn = shape_dn;
-    p.min_rows = kTcMinRows;
-    p.gemv_skip_gu = shape_gu ? kTcMinRows : 0;
-    p.gemv_skip_dn = shape_dn ? kTcMinRows : 0;
+    p.min_rows = thr;
+    p.gemv_skip_gu = shape_gu ? thr : 0;
+    p.gemv_skip_dn = shape_dn ? thr : 0;
   }
   const int64_t big = p.min_rows ? std::min<int64_t>(E, P / p.min_rows) : std::min<int64_t>(E, P);
   p.max_tiles = (int)(P / moe::kTcTileRows + big + 1);
@@ -479,6 +506,10 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   gu.n_active = ws.n_active;
   gu.out = ws.hbuf;
   gu.out_mode = 0;
+  gu.partial = ws.gemv_partial;
+  gu.partial_bytes = ws.gemv_partial_bytes;
+  gu.part_rows = P;
+  gu.num_experts_total = E;
   MOE_MARK(ev, kGateUp, ctx->stream);
   // GEMV first: at decode sizes it carries the work, and the (mostly idle) tcgen05
   // launch behind it overlaps its tail under programmatic dependent launch.
@@ -501,6 +532,10 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   dn.n_active = ws.n_active;
   dn.out = ws.ybuf;
   dn.out_mode = 0;
+  dn.partial = ws.gemv_partial;
+  dn.partial_bytes = ws.gemv_partial_bytes;
+  dn.part_rows = P;
+  dn.num_experts_total = E;
   MOE_MARK(ev, kDown, ctx->stream);
   if (plan.gemv_dn) {
     dn.max_expert_rows = plan.gemv_skip_dn;
@@ -523,6 +558,9 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
     sgu.x_mode = 0;
     sgu.n_identity = (int)T;
     sgu.out = ws.hs;
+    sgu.partial = ws.gemv_partial;
+    sgu.partial_bytes = ws.gemv_partial_bytes;
+    sgu.part_rows = T;
     MOE_MARK(ev, kSharedGateUp, ctx->stream);
     const int stiles = (int)((T + moe::kTcTileRows - 1) / moe::kTcTileRows);
     if (use_tc(T, 1, Is, H)) {
@@ -536,6 +574,9 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
     sdn.x_mode = 0;
     sdn.n_identity = (int)T;
     sdn.out = ws.ys;
+    sdn.partial = ws.gemv_partial;
+    sdn.partial_bytes = ws.gemv_partial_bytes;
+    sdn.part_rows = T;
     MOE_MARK(ev, kSharedDown, ctx->stream);
     if (use_tc(T, 1, H, Is)) {
       moe::TcGemmArgs ta{sdn, nullptr, 1, stiles, ws.status};
@@ -853,6 +894,10 @@ int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_we
   gu.active = ws.active;
   gu.n_active = ws.n_active;
   gu.out = ws.hbuf;
+  gu.partial = ws.gemv_partial;
+  gu.partial_bytes = ws.gemv_partial_bytes;
+  gu.part_rows = P;
+  gu.num_experts_total = El;
   if (plan.gemv_gu) {
     gu.max_expert_rows = plan.gemv_skip_gu;
     MOE_CUDA(ctx, moe::launch_qgemv(gu, true, slots, rows_pe, ctx->stream));
@@ -869,6 +914,10 @@ int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_we
   dn.active = ws.active;
   dn.n_active = ws.n_active;
   dn.out = ws.ybuf;
+  dn.partial = ws.gemv_partial;
+  dn.partial_bytes = ws.gemv_partial_bytes;
+  dn.part_rows = P;
+  dn.num_experts_total = El;
   if (plan.gemv_dn) {
     dn.max_expert_rows = plan.gemv_skip_dn;
     MOE_CUDA(ctx, moe::launch_qgemv(dn, false, slots, rows_pe, ctx->stream));

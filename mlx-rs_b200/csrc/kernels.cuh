@@ -98,6 +98,13 @@ struct QgemvArgs {
   uint16_t* out;            // [rows, N] bf16
   int out_mode;             // 0: row = pos, 1: row = perm[pos]
   int max_expert_rows;      // experts with this many rows or more are skipped (0: none)
+  // split-K (set by launch_qgemv when the grid would be too small): fp32 partials
+  // [ksplit][part_rows][N or 2N] in a caller-provided buffer, then a reduction launch.
+  int ksplit;
+  float* partial;           // null: never split
+  size_t partial_bytes;
+  int64_t part_rows;        // rows of the partial buffer (grouped positions; P or T)
+  int num_experts_total;    // entries of offsets minus one (for the reduction's row check)
 };
 
 struct CombineArgs {

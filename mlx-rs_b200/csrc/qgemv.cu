@@ -29,6 +29,7 @@
 // 16c+8+j, 16c+12+j. The staged token rows are stored in exactly that order, so a
 // lane's B fragments for a group are two 16-byte shared loads.
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -111,7 +112,7 @@ struct RowMap {
 //   rings [warps][NS][MT*16 rows][128 B]  weight chunks; the 32-byte group slot of
 //         ring row r is stored at slot (group ^ (r & 3)), which keeps the lanes' 8-byte
 //         fragment reads conflict-free.
-template <bool GATED, int MT, int NC, int NS>
+template <bool GATED, int MT, int NC, int NS, bool SPLIT>
 __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_expert, int ctas_per_expert,
                                                     int max_slots) {
   constexpr int ROWS = GATED ? 8 * MT : 16 * MT;  // output rows per unit
@@ -122,8 +123,12 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
   extern __shared__ __align__(16) unsigned char smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int gq = lane >> 2, cq = lane & 3;
-  const int slot = blockIdx.x / ctas_per_expert;
-  const int ut = (blockIdx.x - slot * ctas_per_expert) * nwarps + warp;
+  // blockIdx.x = (slot * ksplit + ks) * ctas_per_expert + cta within the expert
+  const int ksplit = SPLIT ? a.ksplit : 1;
+  const int slot = blockIdx.x / (ctas_per_expert * ksplit);
+  const int rem = blockIdx.x - slot * ctas_per_expert * ksplit;
+  const int ks = SPLIT ? rem / ctas_per_expert : 0;
+  const int ut = (rem - ks * ctas_per_expert) * nwarps + warp;
   pdl_wait();
   if (slot >= max_slots) return;
   if (a.n_active && slot >= *a.n_active) return;
@@ -175,6 +180,17 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
   }
   const int nchunks = (G + kKC - 1) / kKC;
   const int tail_groups = G - (nchunks - 1) * kKC;  // groups in the last chunk
+  // split-K: this CTA covers chunks [c_begin, c_end) of K (the host makes every split
+  // non-empty); sources start at c_begin
+  const int cpk = SPLIT ? (nchunks + ksplit - 1) / ksplit : nchunks;
+  const int c_begin = SPLIT ? ks * cpk : 0;
+  const int c_end = SPLIT ? ((c_begin + cpk < nchunks) ? c_begin + cpk : nchunks) : nchunks;
+  const int g_begin = SPLIT ? c_begin * kKC : 0;
+  const int g_end = SPLIT ? ((c_end * kKC < G) ? c_end * kKC : G) : G;
+  if (SPLIT) {
+#pragma unroll
+    for (int i = 0; i < kPieces; ++i) src[i] += (size_t)c_begin * kKC * 8;
+  }
   int issued = 0;  // chunks issued so far in this token chunk
   auto reset_src = [&]() {
 #pragma unroll
@@ -230,19 +246,20 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
     if (unit_live) {
 #pragma unroll
       for (int i = 0; i < NS - 1; ++i) {
-        if (i < nchunks) issue_chunk(i);
+        if (c_begin + i < c_end) issue_chunk(c_begin + i);
         else cp_commit();
       }
     }
     __syncthreads();  // the previous chunk's readers of xperm/xsum are done
     // ---- stage the token rows: fragment-order permutation + per-group sums
-    const int units = ntok * G * 4;
+    const int GS = g_end - g_begin;  // groups of this K split
+    const int units = ntok * GS * 4;
     for (int u0 = 0; u0 < units; u0 += blockDim.x) {  // uniform trip count (shuffles below)
       const int u = u0 + tid;
       const bool uvalid = u < units;
       const int c = u & 3;
-      const int g = (u >> 2) % G;
-      const int t = (u >> 2) / G;
+      const int g = g_begin + (u >> 2) % GS;
+      const int t = (u >> 2) / GS;
       uint32_t in[8];
       if (uvalid) {
         const uint4* p = reinterpret_cast<const uint4*>(a.x + (size_t)rm.xrow(cbase + t) * K + g * 64 + c * 16);
@@ -315,12 +332,12 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
           }
         }
     };
-    load_scales(0, sw, bw);
-    for (int c = 0; c < nchunks; ++c) {
-      if (c + NS - 1 < nchunks) issue_chunk(c + NS - 1);
+    load_scales(c_begin, sw, bw);
+    for (int c = c_begin; c < c_end; ++c) {
+      if (c + NS - 1 < c_end) issue_chunk(c + NS - 1);
       else cp_commit();
       uint32_t swn[MT][2][2], bwn[MT][2][2];
-      if (c + 1 < nchunks) load_scales(c + 1, swn, bwn);
+      if (c + 1 < c_end) load_scales(c + 1, swn, bwn);
       const int g0 = c * kKC;
       cp_wait<NS - 1>();
       __syncwarp();
@@ -373,7 +390,7 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
         }
       }
       __syncwarp();  // every lane is done with this stage before it is refilled
-      if (c + 1 < nchunks) {
+      if (c + 1 < c_end) {
 #pragma unroll
         for (int t = 0; t < MT; ++t)
 #pragma unroll
@@ -389,6 +406,34 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
     pdl_trigger();
 
     // ---- epilogue: C fragment (MMA rows gq / gq+8, tokens 2cq / 2cq+1 of each chunk)
+    if (SPLIT) {
+      // fp32 partial sums of this K split: [ks][pos][N] (plain) or [ks][pos][gate N | up N]
+      const int N2 = GATED ? 2 * N : N;
+#pragma unroll
+      for (int n = 0; n < NC; ++n)
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          const int tok = n * kTok + 2 * cq + cc;
+          if (tok < ntok) {
+            float* pr = a.partial + ((size_t)ks * a.part_rows + (size_t)(cbase + tok)) * N2;
+#pragma unroll
+            for (int t = 0; t < MT; ++t) {
+              if (GATED) {
+                const int row = r0 + 8 * t + gq;
+                if (row < N) {
+                  pr[row] = acc[n][t][cc];
+                  pr[N + row] = acc[n][t][2 + cc];
+                }
+              } else {
+                const int row = r0 + 16 * t + gq;
+                if (row < N) pr[row] = acc[n][t][cc];
+                if (row + 8 < N) pr[row + 8] = acc[n][t][2 + cc];
+              }
+            }
+          }
+        }
+      continue;
+    }
 #pragma unroll
     for (int n = 0; n < NC; ++n)
 #pragma unroll
@@ -414,18 +459,52 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
   }
 }
 
-template <bool GATED, int MT, int NC, int NS>
-static cudaError_t launch_qgemv_t(const QgemvArgs& a, int slots, int wpc, cudaStream_t st) {
-  constexpr int ROWS = GATED ? 8 * MT : 16 * MT;
-  const int upe = (a.N + ROWS - 1) / ROWS;
-  const int cpe = (upe + wpc - 1) / wpc;
-  const long long blocks = (long long)cpe * slots;
+// Split-K reduction: out[row(pos), n] from the ksplit fp32 partials, added in split
+// order, then SwiGLU (gated, the exact bf16 sequence of the GEMV epilogue) or bf16
+// rounding. Rows of experts that the GEMV skipped (max_expert_rows) are left alone.
+template <bool GATED>
+__global__ void __launch_bounds__(256) qgemv_reduce_kernel(QgemvArgs a, int num_slots_e) {
+  const int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  const int N = a.N;
+  if (id >= a.part_rows * N) return;
+  const int64_t pos = id / N;
+  const int n = (int)(id - pos * N);
+  if (a.offsets) {
+    const int64_t valid = a.offsets[num_slots_e];
+    if (pos >= valid) return;
+    if (a.max_expert_rows) {
+      int l = 0, r = num_slots_e;  // expert e with offsets[e] <= pos < offsets[e + 1]
+      while (r - l > 1) {
+        const int m = (l + r) >> 1;
+        if (a.offsets[m] <= pos) l = m;
+        else r = m;
+      }
+      if (a.offsets[l + 1] - a.offsets[l] >= a.max_expert_rows) return;
+    }
+  }
+  const int N2 = GATED ? 2 * N : N;
+  float g = 0.0f, u = 0.0f;
+  for (int k = 0; k < a.ksplit; ++k) {
+    const float* pr = a.partial + ((size_t)k * a.part_rows + pos) * N2;
+    g = __fadd_rn(g, pr[n]);
+    if (GATED) u = __fadd_rn(u, pr[N + n]);
+  }
+  RowMap rm{a.x_mode, a.x_repeat, a.lhs, a.perm};
+  const int64_t orow = a.out_mode == 0 ? pos : rm.orig(pos);
+  a.out[(size_t)orow * N + n] = GATED ? swiglu_bf16(rbf(g), rbf(u)) : f2bf(g);
+}
+
+template <bool GATED, int MT, int NC, int NS, bool SPLIT>
+static cudaError_t launch_split_t(const QgemvArgs& a, int upe, int cpe, int slots, int wpc, cudaStream_t st) {
+  const long long blocks = (long long)cpe * slots * a.ksplit;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   const int G = a.K / 64;
   const size_t smem = (size_t)kTok * NC * (2 * a.K + 16) + (size_t)G * kTok * NC * 4 +
                       (size_t)wpc * NS * MT * 16 * kKC * 32;
   if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
-  auto kern = qgemv_kernel<GATED, MT, NC, NS>;
+  auto kern = qgemv_kernel<GATED, MT, NC, NS, SPLIT>;
   static thread_local int set_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -435,6 +514,40 @@ static cudaError_t launch_qgemv_t(const QgemvArgs& a, int slots, int wpc, cudaSt
     set_dev = dev;
   }
   return launch_k(kern, dim3((unsigned)blocks), dim3(wpc * 32), smem, st, a, upe, cpe, slots);
+}
+
+template <bool GATED, int MT, int NC, int NS>
+static cudaError_t launch_qgemv_t(const QgemvArgs& a0, int slots, int wpc, cudaStream_t st) {
+  constexpr int ROWS = GATED ? 8 * MT : 16 * MT;
+  QgemvArgs a = a0;
+  const int upe = (a.N + ROWS - 1) / ROWS;
+  const int cpe = (upe + wpc - 1) / wpc;
+  // Split K when the units of work would leave most of the GPU idle (few experts and
+  // few rows: the shared expert, or T <= a few tokens) and the partials fit the buffer.
+  a.ksplit = 1;
+  {
+    const int nchunks = (a.K / 64 + kKC - 1) / kKC;
+    const long long warps = (long long)slots * cpe * wpc;
+    int ks = 1;
+    // only when under an eighth of the GPU's warp slots would be busy (the Qwen1.5 shared
+    // expert at T=1: 128 warps): a split adds a reduction launch and a round trip of fp32
+    // partials, which measured slower already at 512 warps (LFM2 down projection, T=1)
+    if (warps * 8 <= 148LL * 16)
+      while (ks < 8 && warps * ks * 2 <= 148LL * 16 && 2 * ks <= nchunks) ks *= 2;
+    const char* env = std::getenv("MOE_B200_SPLITK");  // "0": never split (tests compare both)
+    if (ks > 1 && a.partial && a.part_rows > 0 && !(env && env[0] == '0')) {
+      const int cpk = (nchunks + ks - 1) / ks;
+      ks = (nchunks + cpk - 1) / cpk;  // every split non-empty
+      const size_t need = (size_t)ks * a.part_rows * (GATED ? 2 : 1) * a.N * sizeof(float);
+      if (ks > 1 && need <= a.partial_bytes) a.ksplit = ks;
+    }
+  }
+  cudaError_t err = a.ksplit > 1 ? launch_split_t<GATED, MT, NC, NS, true>(a, upe, cpe, slots, wpc, st)
+                                  : launch_split_t<GATED, MT, NC, NS, false>(a, upe, cpe, slots, wpc, st);
+  if (err != cudaSuccess || a.ksplit == 1) return err;
+  const long long n = a.part_rows * (long long)a.N;
+  return launch_k(qgemv_reduce_kernel<GATED>, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, a,
+                  a.num_experts_total);
 }
 
 template <bool GATED, int NC>

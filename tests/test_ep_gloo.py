@@ -40,19 +40,20 @@ def _worker(rank, world, port, case, q):
         from parity import assert_close
 
         res = {}
-        if case in ("block", "sigmoid"):
-            cfg = CFG if case == "block" else CFG_SIG
+        if case in ("block", "sigmoid", "chunked"):
+            cfg = CFG if case != "sigmoid" else CFG_SIG
             bw = S.host_block(cfg, 41)
-            T_r = 5
+            T_r = 6 if case == "chunked" else 5
             x = S.host_x(41, world * T_r, cfg.hidden)
             e0, n = expert_range(cfg.num_experts, world, rank)
-            blk = ExpertParallelBlock(local_block(bw, e0, n), cfg, expert_begin=e0, num_local=n, ops=OracleEpOps())
+            blk = ExpertParallelBlock(local_block(bw, e0, n), cfg, expert_begin=e0, num_local=n, ops=OracleEpOps(),
+                                      chunks=3 if case == "chunked" else None)
             xr = from_bits(x[rank * T_r:(rank + 1) * T_r])
             out = blk.forward(xr)
             ref, idx, w = O.block_forward(bw, x)
             rows = slice(rank * T_r, (rank + 1) * T_r)
-            pk = blk.buffers(T_r, xr.device).packed_all.numpy().view(np.uint32)
-            assert np.array_equal(pk, O.pack_routing(idx, w)), "routing differs"
+            pk = blk.buffers(T_r, xr.device).packed.numpy().view(np.uint32)
+            assert np.array_equal(pk, O.pack_routing(idx, w)[rows]), "routing differs"
             m = assert_close(bits(out), ref[rows], f"ep rank {rank}")
             res = {"frac_exact": m["frac_exact"]}
         elif case == "stack":
@@ -109,6 +110,12 @@ def test_ep_block_matches_single_device_oracle(world):
 
 def test_ep_sigmoid_routing_world2():
     _run("sigmoid", 2)
+
+
+def test_ep_chunked_overlap_world2():
+    """Three token chunks per block: gathers and all-to-alls issued asynchronously so that
+    they overlap the next chunk's experts; same results as the single-device block."""
+    _run("chunked", 2)
 
 
 def test_ep_stack_with_fused_norm_world2():

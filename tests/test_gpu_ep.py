@@ -148,6 +148,12 @@ def _nccl_worker(rank, world, port, q):
         y = stack(x_all[rows].contiguous())
         torch.cuda.synchronize()
         res["stack_finite"] = bool(torch.isfinite(y.float()).all())
+        # the same block in two token chunks (collectives overlapped with the experts)
+        eps[0].chunks = 2
+        out2 = eps[0](x_all[rows].contiguous())
+        torch.cuda.synchronize()
+        m2 = assert_close(dev_bits(out2), dev_bits(ref)[rows], f"nccl chunked rank {rank}", ULP_TOL)
+        res["frac_exact_chunked"] = m2["frac_exact"]
         q.put((rank, "ok", res))
     except Exception:
         import traceback
@@ -185,3 +191,4 @@ def test_ep_nccl_multi_gpu():
         st, payload = results[r]
         assert st == "ok", f"rank {r}:\n{payload}"
         assert payload["frac_exact"] > 0.99 and payload["stack_finite"], payload
+        assert payload["frac_exact_chunked"] > 0.99, payload
