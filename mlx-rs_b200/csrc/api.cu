@@ -130,8 +130,28 @@ struct BlockWs {
   int32_t* status;
   float* gemv_partial;  // split-K partials of small GEMVs (null when T is large)
   size_t gemv_partial_bytes;
+  float* tc_partial;    // split-K partials of the shared expert's tcgen05 GEMMs
+  size_t tc_partial_bytes;
   size_t bytes;
 };
+
+// K splits of a single-matrix tcgen05 GEMM (the shared expert) whose ctas CTAs would
+// leave SMs idle: up to 8, about two waves of CTAs, at least 4 K steps per split, and
+// partials [splits][rows][N2] fp32 within cap bytes.
+int tc_ksplit(int ctas, int ksteps, int64_t rows, int N2, size_t cap) {
+  if (ctas >= 148 || cap == 0) return 1;
+  int ks = 1;
+  while (ks < 8 && (int64_t)ctas * ks * 2 <= 2 * 148 && ksteps / (2 * ks) >= 4) ks *= 2;
+  while (ks > 1 && (size_t)ks * rows * N2 * sizeof(float) > cap) ks >>= 1;
+  return ks;
+}
+
+// Shared-expert split-K buffer at prefill sizes (the down projection): at most 64 MiB.
+size_t tc_partial_floats(const moe_block_config* c, int64_t T) {
+  if (c->shared_inter <= 0 || T < 32) return 0;
+  const size_t want = (size_t)8 * T * c->hidden;
+  return std::min<size_t>(want, (size_t)16 << 20);
+}
 
 // Split-K partial buffer of a block call: up to 8 splits of the routed projections
 // (P <= 256 pairs) and of the shared expert (T <= 64 tokens); 0 when neither applies.
@@ -171,6 +191,9 @@ BlockWs carve_block(void* base, const moe_block_config* c, int64_t T) {
   const size_t npart = gemv_partial_floats(c, T);
   w.gemv_partial = npart ? cv.take<float>(npart) : nullptr;
   w.gemv_partial_bytes = npart * sizeof(float);
+  const size_t ntc = tc_partial_floats(c, T);
+  w.tc_partial = ntc ? cv.take<float>(ntc) : nullptr;
+  w.tc_partial_bytes = ntc * sizeof(float);
   w.bytes = cv.off + 256;
   return w;
 }
@@ -420,7 +443,7 @@ struct ExpertPlan {
   int max_tiles = 0;                      // tcgen05 grid.y
 };
 
-ExpertPlan plan_experts(int64_t P, int E, int I, int H) {
+ExpertPlan plan_experts(int64_t P, int E, int I, int H, int E_local) {
   ExpertPlan p;
   const bool shape_gu = I % 128 == 0 && H % 64 == 0, shape_dn = H % 128 == 0 && I % 64 == 0;
   const char* v = std::getenv("MOE_B200_TC");
@@ -439,7 +462,11 @@ ExpertPlan plan_experts(int64_t P, int E, int I, int H) {
   } else if (P >= kTcMinRows) {
     const int64_t avg = (P + E - 1) / E;
     const int pass = 8 * (avg > 16 ? 4 : avg > 8 ? 2 : 1);  // tokens per GEMV pass
-    const int thr = std::max(kTcMinRows, 3 * pass);
+    // With enough local experts the tcgen05 CTAs (one per expert x 128 gate/up rows) fill
+    // the GPU and every expert from 32 rows up goes there; with few (expert parallelism on
+    // many GPUs) they would not, and the GEMV keeps experts of up to three passes.
+    const bool fills = (int64_t)E_local * (I / 128) >= 148;
+    const int thr = fills ? kTcMinRows : std::max(kTcMinRows, 3 * pass);
     p.tc_gu = shape_gu;
     p.tc_dn = shape_dn;
     p.min_rows = thr;
@@ -488,7 +515,7 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   BlockWs ws = carve_block(ctx->scratch, cfg, T);
   const int E = cfg->num_experts, H = cfg->hidden, I = cfg->moe_inter, k = cfg->top_k;
   const int64_t P = T * k;
-  const ExpertPlan plan = plan_experts(P, E, I, H);
+  const ExpertPlan plan = plan_experts(P, E, I, H, E);
   rc = run_route(ctx, cfg, wts, x, T, ws, ev, nullptr, plan.min_rows);
   if (rc) return rc;
 
@@ -565,6 +592,8 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
     const int stiles = (int)((T + moe::kTcTileRows - 1) / moe::kTcTileRows);
     if (use_tc(T, 1, Is, H)) {
       moe::TcGemmArgs ta{sgu, nullptr, 1, stiles, ws.status};
+      // (not split: the gated partials are twice as wide and measured slower split,
+      // 84 us against 49 us for Qwen1.5-MoE at T=512)
       MOE_CUDA(ctx, moe::launch_tc_gemm(ta, true, ctx->stream));
     } else {
       MOE_CUDA(ctx, moe::launch_qgemv(sgu, true, 1, (int)T, ctx->stream));
@@ -580,6 +609,9 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
     MOE_MARK(ev, kSharedDown, ctx->stream);
     if (use_tc(T, 1, H, Is)) {
       moe::TcGemmArgs ta{sdn, nullptr, 1, stiles, ws.status};
+      ta.q.partial = ws.tc_partial;
+      ta.q.partial_bytes = ws.tc_partial_bytes;
+      ta.ksplit = tc_ksplit((H % 256 == 0 ? H / 256 : H / 128) * stiles, Is / 64, T, H, ws.tc_partial_bytes);
       MOE_CUDA(ctx, moe::launch_tc_gemm(ta, false, ctx->stream));
     } else {
       MOE_CUDA(ctx, moe::launch_qgemv(sdn, false, 1, (int)T, ctx->stream));
@@ -876,7 +908,7 @@ int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_we
   // Path choice per expert as in moe_block_forward, on the expected rows per expert of
   // all pairs over all E experts; the grids cover every local pair in the worst case
   // and idle CTAs leave at once.
-  ExpertPlan plan = plan_experts(P, E, I, H);
+  ExpertPlan plan = plan_experts(P, E, I, H, El);
   plan.max_tiles = (int)(P / moe::kTcTileRows +
                          std::min<int64_t>(El, plan.min_rows ? P / plan.min_rows : P) + 1);
   ga.tile_start = ws.tile_start;

@@ -150,7 +150,10 @@ struct TcGemmArgs {
   int num_experts;            // E (entries of tile_start minus one)
   int max_tiles;              // grid.y
   int32_t* status;            // device word: nonzero after a bounded wait expired
+  int ksplit;                 // grid.z: K splits into q.partial (identity rows only), 0/1 none
 };
+// Ordered reduction of split-K partials (q.partial, q.ksplit, q.part_rows) into q.out.
+cudaError_t launch_gemv_reduce(const QgemvArgs& q, bool gated, cudaStream_t st);
 constexpr int kTcTileRows = 256;
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, bool gated, cudaStream_t st);
 

@@ -6,17 +6,17 @@
 //
 // One CTA computes D[128 weight rows x n tokens] = W_tile . X_tile^T over the whole K
 // for one expert and one tile of up to 256 of its (grouped) token rows:
-//   * warps 0-7 (256 threads) are producers: per K step of 64 (one quantization group)
-//     thread p loads 32 packed int4 elements of weight row p/2 (half p%2 of the group),
+//   * warps 0-15 (512 threads) are producers: per K step of 64 (one quantization group)
+//     thread p loads 16 packed int4 elements of weight row p/4 (quarter p%4 of the group),
 //     dequantises them to bf16 (w = RN_bf16(s*q + b), the value MLX's GPU qmm computes
 //     into threadgroup memory) and stores them into the A tile, and copies its share of
 //     the token rows with cp.async into the B tile; both tiles are K-major with the
 //     128-byte swizzle the tensor core reads;
-//   * warp 8 allocates tensor memory and, from one lane, issues tcgen05.mma
+//   * warp 16 allocates tensor memory and, from one lane, issues tcgen05.mma
 //     (kind::f16, bf16 x bf16 -> fp32, M=128, N=n rounded up to 16, K=16 per instruction)
 //     accumulating in TMEM; tcgen05.commit on an mbarrier frees each stage;
 //   * after the last stage the producer warps read the accumulators back with
-//     tcgen05.ld (warp w owns TMEM lanes 32(w%4).. = weight rows, and every other block
+//     tcgen05.ld (warp w owns TMEM lanes 32(w%4).. = weight rows, and every fourth block
 //     of 32 token columns by w/4); in the gated form the gate and up accumulators (TMEM
 //     columns 0 and 256) are combined by SwiGLU in registers (bf16 multiplies exact as in
 //     the reference; the sigmoid from the hardware ex2/rcp approximations, which is why
@@ -37,17 +37,22 @@ constexpr int kBN = kTcTileRows;           // max tokens per CTA (MMA N)
 constexpr int kBK = 64;                    // K per stage
 constexpr int kATileBytes = kBM * kBK * 2;   // 16 KB
 constexpr int kBTileBytes = kBN * kBK * 2;   // 32 KB
-constexpr int kProducers = 256;
+constexpr int kProducers = 512;
+constexpr int kParts = kProducers / kBM;    // producer threads per weight row (4)
+constexpr int kWords = 8 / kParts;          // packed words of a group each handles (2)
+constexpr int kColGroups = kProducers / 128;  // epilogue: warps sharing a TMEM lane quadrant
 constexpr int kMmaWarp = kProducers / 32;
 constexpr int kThreads = kProducers + 32;
 constexpr uint64_t kWaitLimitNs = 200ull * 1000 * 1000;  // bound of one mbarrier wait (200 ms)
 
-template <bool GATED>
+// MODE 0: plain, 128 weight rows per CTA; 1: gated (gate and up rows); 2: plain, 256
+// weight rows per CTA as two 128-row accumulators (halves the token-tile reloads).
+template <int MODE>
 struct TcCfg {
-  static constexpr int kMats = GATED ? 2 : 1;
-  static constexpr int kStages = GATED ? 3 : 4;
+  static constexpr int kMats = MODE ? 2 : 1;
+  static constexpr int kStages = MODE ? 3 : 4;
   static constexpr int kStageBytes = kMats * kATileBytes + kBTileBytes;
-  static constexpr int kTmemCols = GATED ? 512 : 256;
+  static constexpr int kTmemCols = MODE ? 512 : 256;
   // [stages][A tiles..., B tile] | full[S] empty[S] done | tmem base | xrow[kBN]
   static constexpr int kBarOffset = kStages * kStageBytes;
   static constexpr int kSmemBytes = kBarOffset + 8 * (2 * kStages + 1) + 16 + 4 * kBN + 1024;
@@ -142,6 +147,16 @@ MOE_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
 
+MOE_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+
 // bf16 pair (128 + q_j, 128 + q_{j+4}) from nibbles j and j+4 of w.
 MOE_DEV uint32_t nib_pair(uint32_t w, int j) {
   uint32_t r;
@@ -227,9 +242,11 @@ struct RowMap {
 
 }  // namespace
 
-template <bool GATED>
+template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
-  using C = TcCfg<GATED>;
+  using C = TcCfg<MODE>;
+  constexpr bool GATED = MODE == 1;
+  constexpr int kRowsPerCta = MODE == 2 ? 2 * kBM : kBM;
   const QgemvArgs& a = ta.q;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -242,8 +259,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
   __shared__ int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int K = a.K, N = a.N, G = K >> 6, wpr = K >> 3;
-  const int n0 = blockIdx.x * kBM;
+  const int K = a.K, N = a.N, Gtot = K >> 6, wpr = K >> 3;
+  // split-K (blockIdx.z): this CTA accumulates K steps [G0, G0 + G) of the Gtot
+  const int ksp = ta.ksplit > 1 ? ta.ksplit : 1;
+  const int spk = (Gtot + ksp - 1) / ksp;
+  const int G0 = (int)blockIdx.z * spk;
+  const int G = (G0 + spk < Gtot ? G0 + spk : Gtot) - G0;
+  const int n0 = blockIdx.x * kRowsPerCta;
 
   pdl_wait();
   // ---- map blockIdx.y to (expert, token tile)
@@ -295,30 +317,33 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
 
   if (warp < kMmaWarp) {
     // ================= producers (then epilogue) =================
-    const int p = tid;          // 0..255
-    const int half = p & 1;     // which 32 elements of the row's group of 64
-    const int row = p >> 1;     // weight row within the tile
+    const int p = tid;               // 0..kProducers-1
+    const int part = p % kParts;     // which kWords words (8 elements each) of the row's group
+    const int row = p / kParts;      // weight row within the tile
     const uint32_t* wrow[C::kMats];
     const uint16_t* srow[C::kMats];
     const uint16_t* brow[C::kMats];
 #pragma unroll
     for (int m = 0; m < C::kMats; ++m) {
-      const size_t grow = (size_t)e * N + n0 + row;
-      const uint32_t* W = m ? a.w1 : a.w0;
-      const uint16_t* S = m ? a.s1 : a.s0;
-      const uint16_t* B = m ? a.b1 : a.b0;
-      wrow[m] = W + grow * wpr + half * 4;
-      srow[m] = S + grow * G;
-      brow[m] = B ? B + grow * G : nullptr;
+      const size_t grow = (size_t)e * N + n0 + (MODE == 2 ? m * kBM : 0) + row;
+      const bool second = GATED && m;
+      const uint32_t* W = second ? a.w1 : a.w0;
+      const uint16_t* S = second ? a.s1 : a.s0;
+      const uint16_t* B = second ? a.b1 : a.b0;
+      wrow[m] = W + grow * wpr + (size_t)G0 * 8 + part * kWords;
+      srow[m] = S + grow * Gtot + G0;
+      brow[m] = B ? B + grow * Gtot + G0 : nullptr;
     }
-    // register ring of packed weights + (scale | bias << 16), 2 stages ahead
-    uint4 wr[3][C::kMats];
-    uint32_t sr[3][C::kMats];
+    // register ring of packed weights + (scale | bias << 16), kRing - 1 stages ahead
+    static_assert(kWords == 2, "the loads below move 2 words per matrix");
+    constexpr int kRing = 4;
+    uint2 wr[kRing][C::kMats];
+    uint32_t sr[kRing][C::kMats];
     auto load_w = [&](int slot3, int kk) {
       if (kk < G) {
 #pragma unroll
         for (int m = 0; m < C::kMats; ++m) {
-          wr[slot3][m] = __ldg(reinterpret_cast<const uint4*>(wrow[m] + (size_t)kk * 8));
+          wr[slot3][m] = __ldg(reinterpret_cast<const uint2*>(wrow[m] + (size_t)kk * 8));
           const uint32_t sv = __ldg(srow[m] + kk);
           const uint32_t bv = brow[m] ? __ldg(brow[m] + kk) : 0u;
           sr[slot3][m] = sv | (bv << 16);
@@ -327,19 +352,19 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
     };
     auto issue_b = [&](int kk) {
       const uint32_t bt = sbase + (kk % C::kStages) * C::kStageBytes + C::kMats * kATileBytes;
-      // 256 rows x 8 chunks of 16 bytes; this thread: chunks q = p + 256 i
+      // 256 rows x 8 chunks of 16 bytes; this thread: chunks q = p + kProducers i
 #pragma unroll
       for (int i = 0; i < kBN * 8 / kProducers; ++i) {
         const int q = p + kProducers * i;
         const int r = q >> 3, c = q & 7;
-        if (r < ntok) cp_async16(bt + sw128_off(r, c), a.x + (size_t)xrow_s[r] * K + kk * kBK + c * 8);
+        if (r < ntok) cp_async16(bt + sw128_off(r, c), a.x + (size_t)xrow_s[r] * K + (G0 + kk) * kBK + c * 8);
       }
       cp_commit();
     };
     constexpr int LA = C::kStages - 1;  // B tiles issued this many stages ahead
     bool ok = true;
-    load_w(0, 0);
-    load_w(1, 1);
+#pragma unroll
+    for (int i = 0; i < kRing - 1; ++i) load_w(i, i);
     for (int kk = 0; kk < LA; ++kk) {
       if (kk < G) {
         // fresh barriers: the first wait on "empty" passes immediately
@@ -348,9 +373,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
         cp_commit();
       }
     }
-    for (int kb = 0; kb < G && ok; kb += 3) {
+    for (int kb = 0; kb < G && ok; kb += kRing) {
 #pragma unroll
-      for (int r3 = 0; r3 < 3; ++r3) {
+      for (int r3 = 0; r3 < kRing; ++r3) {
         const int kk = kb + r3;
         if (kk < G && ok) {
           const int s = kk % C::kStages;
@@ -360,18 +385,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
           for (int m = 0; m < C::kMats; ++m) {
             const uint32_t sv = sr[r3][m] & 0xffffu, bv = sr[r3][m] >> 16;
             const uint32_t s2 = sv | (sv << 16), b2 = bv | (bv << 16);
-            const uint4 wv = wr[r3][m];
-            const uint32_t ws[4] = {wv.x, wv.y, wv.z, wv.w};
+            const uint2 wv = wr[r3][m];
+            const uint32_t ws[2] = {wv.x, wv.y};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < kWords; ++j) {
               const uint4 o = dequant8(ws[j], s2, b2);
-              const uint32_t dst = st + m * kATileBytes + sw128_off(row, half * 4 + j);
+              const uint32_t dst = st + m * kATileBytes + sw128_off(row, part * kWords + j);
               asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(dst), "r"(o.x), "r"(o.y), "r"(o.z),
                            "r"(o.w)
                            : "memory");
             }
           }
-          load_w((r3 + 2) % 3, kk + 2);
+          load_w((r3 + kRing - 1) % kRing, kk + kRing - 1);
           // B(kk) landed: at most LA-1 newer groups may still be pending
           cp_wait<LA - 1>();
           fence_proxy_async();
@@ -398,14 +423,52 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
     if (!done_ok && lane == 0) atomicOr(&abort_flag, 2);
     tc_fence_after();
     pdl_trigger();
-    if (done_ok) {
+    if (done_ok && ksp > 1) {
+      // split-K: fp32 partials [kz][pos][N] (plain) or [kz][pos][gate N | up N] (gated),
+      // added in split order and finished by the GEMV's reduction kernel
+      const int quad = warp & 3;
+      const uint32_t tl = tmem + ((uint32_t)(32 * quad) << 16);
+      const int N2 = GATED ? 2 * N : N;
+      for (int c0 = 32 * (warp >> 2); c0 < nmma; c0 += 32 * kColGroups) {
+#pragma unroll 1
+        for (int m = 0; m < C::kMats; ++m) {
+          const int col = (GATED ? m * N : (MODE == 2 ? m * kBM : 0)) + n0 + 32 * quad + lane;
+          float* base = a.partial + ((size_t)blockIdx.z * a.part_rows + (size_t)tbeg) * N2 + col;
+#pragma unroll 1
+          for (int h = 0; h < 32; h += 16) {
+            uint32_t g[16];
+            tmem_ld16(tl + m * 256 + c0 + h, g);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (c0 + h + j < ntok) base[(size_t)(c0 + h + j) * N2] = __uint_as_float(g[j]);
+          }
+        }
+      }
+    } else if (done_ok) {
       // Every MMA has completed, so the stage buffers are free: each warp transposes its
       // 32 rows x 32 tokens tile through 2 KB of stage 0.
       const int quad = warp & 3;                    // TMEM lanes 32*quad.. (weight rows)
       const uint32_t tl = tmem + ((uint32_t)(32 * quad) << 16);
       unsigned char* tile = smem + warp * 2048;     // [32 tokens][32 rows] bf16
       const uint32_t tile_s = sbase + warp * 2048;
-      for (int c0 = 32 * (warp >> 2); c0 < nmma; c0 += 64) {
+      // token row t of the tile = 64 bytes = 4 x 16 bytes; lane -> (t = lane/4 + 8i, piece
+      // lane%4); col_off selects the 128-row accumulator (MODE 2)
+      int c0 = 0;
+      auto store_tile = [&](int col_off) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int t = (lane >> 2) + 8 * i;
+          const int tok = c0 + t;
+          if (tok < ntok) {
+            const uint4 v = lds_v4(tile_s + t * 64 + (lane & 3) * 16);
+            const int64_t pos = tbeg + tok;
+            const int64_t orow = a.out_mode == 0 ? pos : rm.orig(pos);
+            *reinterpret_cast<uint4*>(a.out + (size_t)orow * N + n0 + col_off + 32 * quad + (lane & 3) * 8) = v;
+          }
+        }
+        __syncwarp();
+      };
+      for (c0 = 32 * (warp >> 2); c0 < nmma; c0 += 32 * kColGroups) {
         uint32_t g[32];
         tmem_ld32(tl + c0, g);
         if (GATED) {
@@ -427,19 +490,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
           }
         }
         __syncwarp();
-        // token row t of the tile = 64 bytes = 4 x 16 bytes; lane -> (t = lane/4 + 8i, piece lane%4)
+        store_tile(0);
+        if (MODE == 2) {  // the second 128-row accumulator
+          tmem_ld32(tl + 256 + c0, g);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int t = (lane >> 2) + 8 * i;
-          const int tok = c0 + t;
-          if (tok < ntok) {
-            const uint4 v = lds_v4(tile_s + t * 64 + (lane & 3) * 16);
-            const int64_t pos = tbeg + tok;
-            const int64_t orow = a.out_mode == 0 ? pos : rm.orig(pos);
-            *reinterpret_cast<uint4*>(a.out + (size_t)orow * N + n0 + 32 * quad + (lane & 3) * 8) = v;
+          for (int j = 0; j < 32; j += 2) {
+            const uint32_t o2 = pack_bf2(__uint_as_float(g[j]), __uint_as_float(g[j + 1]));
+            *reinterpret_cast<uint16_t*>(tile + j * 64 + lane * 2) = (uint16_t)(o2 & 0xffffu);
+            *reinterpret_cast<uint16_t*>(tile + (j + 1) * 64 + lane * 2) = (uint16_t)(o2 >> 16);
           }
+          __syncwarp();
+          store_tile(kBM);
         }
-        __syncwarp();
       }
     }
   } else if (lane == 0) {
@@ -480,26 +542,31 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
   }
 }
 
-template <bool GATED>
+template <int MODE>
 static cudaError_t launch_tc_t(const TcGemmArgs& a, cudaStream_t st) {
-  using C = TcCfg<GATED>;
+  using C = TcCfg<MODE>;
   static thread_local int set_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev != set_dev) {
-    cudaError_t err = cudaFuncSetAttribute(tc_gemm_kernel<GATED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t err = cudaFuncSetAttribute(tc_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            C::kSmemBytes);
     if (err != cudaSuccess) return err;
     set_dev = dev;
   }
-  dim3 grid(a.q.N / kBM, a.max_tiles);
-  return launch_k(tc_gemm_kernel<GATED>, grid, dim3(kThreads), (size_t)C::kSmemBytes, st, a);
+  dim3 grid(a.q.N / (MODE == 2 ? 2 * kBM : kBM), a.max_tiles, a.ksplit > 1 ? a.ksplit : 1);
+  return launch_k(tc_gemm_kernel<MODE>, grid, dim3(kThreads), (size_t)C::kSmemBytes, st, a);
 }
 
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, bool gated, cudaStream_t st) {
   if (a.max_tiles <= 0) return cudaSuccess;
   if (a.q.N % kBM != 0 || a.q.K % kBK != 0) return cudaErrorInvalidValue;
-  return gated ? launch_tc_t<true>(a, st) : launch_tc_t<false>(a, st);
+  cudaError_t err = gated ? launch_tc_t<1>(a, st)
+                          : (a.q.N % (2 * kBM) == 0 ? launch_tc_t<2>(a, st) : launch_tc_t<0>(a, st));
+  if (err != cudaSuccess || a.ksplit <= 1) return err;
+  QgemvArgs r = a.q;
+  r.ksplit = a.ksplit;
+  return launch_gemv_reduce(r, gated, st);
 }
 
 }  // namespace moe

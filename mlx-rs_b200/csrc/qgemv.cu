@@ -550,6 +550,14 @@ static cudaError_t launch_qgemv_t(const QgemvArgs& a0, int slots, int wpc, cudaS
                   a.num_experts_total);
 }
 
+cudaError_t launch_gemv_reduce(const QgemvArgs& a, bool gated, cudaStream_t st) {
+  const long long n = a.part_rows * (long long)a.N;
+  if (n <= 0 || a.ksplit <= 1) return cudaSuccess;
+  const dim3 grid((unsigned)((n + 255) / 256));
+  return gated ? launch_k(qgemv_reduce_kernel<true>, grid, dim3(256), 0, st, a, a.num_experts_total)
+               : launch_k(qgemv_reduce_kernel<false>, grid, dim3(256), 0, st, a, a.num_experts_total);
+}
+
 template <bool GATED, int NC>
 static cudaError_t launch_qgemv_nc(const QgemvArgs& a, int slots, bool wide, cudaStream_t st) {
   return wide ? launch_qgemv_t<GATED, 2, NC, 2>(a, slots, 8, st) : launch_qgemv_t<GATED, 1, NC, 4>(a, slots, 4, st);
