@@ -141,6 +141,16 @@ class ClockSampler:
                 "samples": len(sm), "reasons": sorted(reasons)}
 
 
+# DRAM traffic per launch of the dominant kernel (dram__bytes_read.sum +
+# dram__bytes_write.sum) from one ncu --set full capture of the same workload on a B200.
+NCU_TRAFFIC = {
+    ("decode", "gate_up"): 216_633_856 + 4_721_408,
+    ("decode", "down"): 107_877_376 + 4_674_304,
+    ("prefill", "gate_up"): 262_024_704 + 40_618_240,
+    ("prefill", "down"): 163_624_704 + 99_390_976,
+}
+
+
 def make_workload(args, S, host=True):
     """(config, host weights of block 0 or None, tokens, regime, blocks) of the workload."""
     from dataclasses import replace
@@ -504,6 +514,9 @@ def run_block(args, dev):
     else:
         roof = hbm_roofline(f"qgemv {dom}", alg[dom], stage_ms[dom],
                             {"block_algorithmic_GBps": block_bytes / (ms / 1e3) / 1e9, "stage_ms": stage_ms})
+    if not args.tokens and (args.workload, dom) in NCU_TRAFFIC:
+        roof["traffic"] = NCU_TRAFFIC[(args.workload, dom)]
+        roof["traffic_source"] = "ncu --set full capture of this workload (one launch)"
 
     e2e = e2e_run(args, lambda xd: blk.forward(xd, out), xs_host, (T, H), dev, timer)
 
