@@ -98,6 +98,7 @@ struct QgemvArgs {
   uint16_t* out;            // [rows, N] bf16
   int out_mode;             // 0: row = pos, 1: row = perm[pos]
   int max_expert_rows;      // experts with this many rows or more are skipped (0: none)
+  int min_expert_rows;      // split-K reduction only: experts with fewer rows are skipped (0: none)
   // split-K (set by launch_qgemv when the grid would be too small): fp32 partials
   // [ksplit][part_rows][N or 2N] in a caller-provided buffer, then a reduction launch.
   int ksplit;
@@ -150,7 +151,7 @@ struct TcGemmArgs {
   int num_experts;            // E (entries of tile_start minus one)
   int max_tiles;              // grid.y
   int32_t* status;            // device word: nonzero after a bounded wait expired
-  int ksplit;                 // grid.z: K splits into q.partial (identity rows only), 0/1 none
+  int ksplit;                 // grid.z: K splits into q.partial [ksplit][rows][N or 2N], 0/1 none
 };
 // Ordered reduction of split-K partials (q.partial, q.ksplit, q.part_rows) into q.out.
 cudaError_t launch_gemv_reduce(const QgemvArgs& q, bool gated, cudaStream_t st);

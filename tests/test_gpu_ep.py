@@ -192,3 +192,12 @@ def test_ep_nccl_multi_gpu():
         assert st == "ok", f"rank {r}:\n{payload}"
         assert payload["frac_exact"] > 0.99 and payload["stack_finite"], payload
         assert payload["frac_exact_chunked"] > 0.99, payload
+
+
+def test_ep_world8_tensor_core_split_k():
+    """8 ranks, 64 tokens each: ~32 rows per local expert, so experts from 32 rows go to
+    the tcgen05 kernel, which splits K (16 local experts do not fill the GPU) and adds
+    the fp32 partials in a reduction launch; the smaller experts stay on the GEMV."""
+    _, _, out, ref = _emulate(S.QWEN3_30B_A3B, 1, 64, 8, 340)
+    m = assert_close(out, ref, "EP world 8 split-K vs block", ULP_TOL_TC)
+    assert m["mean_rel"] < 5e-3, m
