@@ -146,8 +146,8 @@ int tc_ksplit(int ctas, int ksteps, int64_t rows, int N2, size_t cap) {
   return ks;
 }
 
-// Split-K buffer of the tcgen05 GEMMs: the shared expert's down projection at prefill
-// sizes, and routed projections when few experts are local; at most 64 MiB.
+// Split-K buffer of the shared expert's tcgen05 down projection at prefill sizes: at
+// most 64 MiB.
 size_t tc_partial_floats(const moe_block_config* c, int64_t T) {
   size_t want = 0;
   if (c->shared_inter > 0 && T >= 32) want = (size_t)8 * T * c->hidden;
@@ -298,8 +298,6 @@ struct EpWs {
   uint16_t *hbuf, *ybuf;
   float* gemv_partial;
   size_t gemv_partial_bytes;
-  float* tc_partial;
-  size_t tc_partial_bytes;
   size_t bytes;
 };
 
@@ -322,11 +320,6 @@ EpWs carve_ep(void* base, const moe_block_config* c, int64_t T, int El) {
   const size_t npart = P <= 256 ? (size_t)8 * P * std::max(2 * c->moe_inter, c->hidden) : 0;
   w.gemv_partial = npart ? cv.take<float>(npart) : nullptr;
   w.gemv_partial_bytes = npart * sizeof(float);
-  // routed tcgen05 split-K with few local experts: up to 4 splits, at most 64 MiB
-  const bool few = (int64_t)El * (c->moe_inter / 128) < 148;
-  const size_t ntc = few ? std::min<size_t>((size_t)4 * P * std::max(2 * c->moe_inter, c->hidden), (size_t)16 << 20) : 0;
-  w.tc_partial = ntc ? cv.take<float>(ntc) : nullptr;
-  w.tc_partial_bytes = ntc * sizeof(float);
   w.bytes = cv.off + 256;
   return w;
 }
@@ -436,12 +429,13 @@ bool use_tc(int64_t rows, int64_t experts, int N, int K) {
 }
 
 // Routed experts: each expert takes the path its own row count calls for, decided on
-// the device. Experts with at least min_rows rows run on the tcgen05 GEMM (the grouping
-// gives only them tiles); the others on the GEMV, which skips the large ones. The GEMV
-// serves 8, 16 or 32 tokens per pass over an expert's weights (by the average rows per
-// expert); an expert that would need more than three passes goes to tcgen05, whose
-// dequantisation into shared memory costs about three GEMV passes. MOE_B200_TC=0 puts
-// every expert on the GEMV, =1 every expert on tcgen05.
+// the device. Experts with at least kTcMinRows rows run on the tcgen05 GEMM (the
+// grouping gives only them tiles); the others on the GEMV, which skips the large ones.
+// (Measured alternatives that were slower: keeping experts of up to three GEMV passes on
+// the GEMV — Qwen1.5-MoE prefill at T=512 fell from 1.14 M to 0.87 M tokens/s — and
+// splitting K of the tcgen05 launches when few experts are local — 8-GPU expert-parallel
+// decode went from 0.265 to 0.300 ms per step.) MOE_B200_TC=0 puts every expert on the
+// GEMV, =1 every expert on tcgen05.
 constexpr int kTcMinRows = 32;
 struct ExpertPlan {
   bool tc_gu = false, tc_dn = false;      // launch the tcgen05 kernel
@@ -449,30 +443,9 @@ struct ExpertPlan {
   int min_rows = 0;                       // tile threshold of the grouping
   int gemv_skip_gu = 0, gemv_skip_dn = 0; // GEMV max_expert_rows
   int max_tiles = 0;                      // tcgen05 grid.y
-  int tc_ks_gu = 1, tc_ks_dn = 1;         // tcgen05 K splits (few local experts)
 };
 
-// Largest power-of-two split <= ks whose partials [ks][rows][N2] fp32 fit in bytes.
-int fit_ksplit(int ks, int64_t rows, int N2, size_t bytes) {
-  while (ks > 1 && (size_t)ks * rows * N2 * sizeof(float) > bytes) ks >>= 1;
-  return ks;
-}
-
-// Split-K of a routed tcgen05 launch: partials over the grouped positions, and the
-// reduction writes only the rows of the experts the tcgen05 kernel handled.
-void set_tc_split(moe::TcGemmArgs& ta, int ks, int min_rows, int64_t rows, int N2, int experts, float* buf,
-                  size_t bytes) {
-  ta.ksplit = buf ? fit_ksplit(ks, rows, N2, bytes) : 1;
-  if (ta.ksplit <= 1) return;
-  ta.q.partial = buf;
-  ta.q.partial_bytes = bytes;
-  ta.q.part_rows = rows;
-  ta.q.num_experts_total = experts;
-  ta.q.max_expert_rows = 0;
-  ta.q.min_expert_rows = min_rows;
-}
-
-ExpertPlan plan_experts(int64_t P, int E, int I, int H, int E_local) {
+ExpertPlan plan_experts(int64_t P, int E, int I, int H) {
   ExpertPlan p;
   const bool shape_gu = I % 128 == 0 && H % 64 == 0, shape_dn = H % 128 == 0 && I % 64 == 0;
   const char* v = std::getenv("MOE_B200_TC");
@@ -494,15 +467,6 @@ ExpertPlan plan_experts(int64_t P, int E, int I, int H, int E_local) {
     p.min_rows = kTcMinRows;
     p.gemv_skip_gu = shape_gu ? kTcMinRows : 0;
     p.gemv_skip_dn = shape_dn ? kTcMinRows : 0;
-    // With few local experts (expert parallelism over many GPUs) one CTA per expert and
-    // 128 (gate/up) or 256 (down) weight rows leaves SMs idle: split K so that about two
-    // CTAs per SM run; the fp32 partials are added in split order by a reduction launch.
-    const int64_t avg = (P + E - 1) / E;
-    const int64_t tiles = std::max<int64_t>(1, avg / moe::kTcTileRows);
-    const int64_t ctas_gu = (int64_t)E_local * (I / 128) * tiles;
-    const int64_t ctas_dn = (int64_t)E_local * (H % 256 == 0 ? H / 256 : H / 128) * tiles;
-    while (p.tc_ks_gu < 4 && ctas_gu * p.tc_ks_gu * 2 <= 2 * 148 && H / 64 >= 8 * p.tc_ks_gu) p.tc_ks_gu *= 2;
-    while (p.tc_ks_dn < 4 && ctas_dn * p.tc_ks_dn * 2 <= 2 * 148 && I / 64 >= 8 * p.tc_ks_dn) p.tc_ks_dn *= 2;
   }
   const int64_t big = p.min_rows ? std::min<int64_t>(E, P / p.min_rows) : std::min<int64_t>(E, P);
   p.max_tiles = (int)(P / moe::kTcTileRows + big + 1);
@@ -546,7 +510,7 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   BlockWs ws = carve_block(ctx->scratch, cfg, T);
   const int E = cfg->num_experts, H = cfg->hidden, I = cfg->moe_inter, k = cfg->top_k;
   const int64_t P = T * k;
-  const ExpertPlan plan = plan_experts(P, E, I, H, E);
+  const ExpertPlan plan = plan_experts(P, E, I, H);
   rc = run_route(ctx, cfg, wts, x, T, ws, ev, nullptr, plan.min_rows);
   if (rc) return rc;
 
@@ -577,7 +541,6 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   }
   if (plan.tc_gu) {
     moe::TcGemmArgs ta{gu, ws.tile_start, E, plan.max_tiles, ws.status};
-    set_tc_split(ta, plan.tc_ks_gu, plan.min_rows, P, 2 * I, E, ws.tc_partial, ws.tc_partial_bytes);
     MOE_CUDA(ctx, moe::launch_tc_gemm(ta, true, ctx->stream));
   }
 
@@ -602,7 +565,6 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   }
   if (plan.tc_dn) {
     moe::TcGemmArgs ta{dn, ws.tile_start, E, plan.max_tiles, ws.status};
-    set_tc_split(ta, plan.tc_ks_dn, plan.min_rows, P, H, E, ws.tc_partial, ws.tc_partial_bytes);
     MOE_CUDA(ctx, moe::launch_tc_gemm(ta, false, ctx->stream));
   }
 
@@ -941,7 +903,7 @@ int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_we
   // Path choice per expert as in moe_block_forward, on the expected rows per expert of
   // all pairs over all E experts; the grids cover every local pair in the worst case
   // and idle CTAs leave at once.
-  ExpertPlan plan = plan_experts(P, E, I, H, El);
+  ExpertPlan plan = plan_experts(P, E, I, H);
   plan.max_tiles = (int)(P / moe::kTcTileRows +
                          std::min<int64_t>(El, plan.min_rows ? P / plan.min_rows : P) + 1);
   ga.tile_start = ws.tile_start;
@@ -969,7 +931,6 @@ int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_we
   }
   if (plan.tc_gu) {
     moe::TcGemmArgs ta{gu, ws.tile_start, El, plan.max_tiles, ws.status};
-    set_tc_split(ta, plan.tc_ks_gu, plan.min_rows, P, 2 * I, El, ws.tc_partial, ws.tc_partial_bytes);
     MOE_CUDA(ctx, moe::launch_tc_gemm(ta, true, ctx->stream));
   }
   moe::QgemvArgs dn = qgemv_args(wts->down, nullptr, H, I);
@@ -990,7 +951,6 @@ int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_we
   }
   if (plan.tc_dn) {
     moe::TcGemmArgs ta{dn, ws.tile_start, El, plan.max_tiles, ws.status};
-    set_tc_split(ta, plan.tc_ks_dn, plan.min_rows, P, H, El, ws.tc_partial, ws.tc_partial_bytes);
     MOE_CUDA(ctx, moe::launch_tc_gemm(ta, false, ctx->stream));
   }
   moe::EpPartialArgs pa{};

@@ -98,7 +98,6 @@ struct QgemvArgs {
   uint16_t* out;            // [rows, N] bf16
   int out_mode;             // 0: row = pos, 1: row = perm[pos]
   int max_expert_rows;      // experts with this many rows or more are skipped (0: none)
-  int min_expert_rows;      // split-K reduction only: experts with fewer rows are skipped (0: none)
   // split-K (set by launch_qgemv when the grid would be too small): fp32 partials
   // [ksplit][part_rows][N or 2N] in a caller-provided buffer, then a reduction launch.
   int ksplit;

@@ -461,8 +461,7 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
 
 // Split-K reduction: out[row(pos), n] from the ksplit fp32 partials, added in split
 // order, then SwiGLU (gated, the exact bf16 sequence of the GEMV epilogue) or bf16
-// rounding. Rows of experts that the splitting kernel did not handle (at least
-// max_expert_rows rows, or fewer than min_expert_rows) are left alone.
+// rounding. Rows of experts that the GEMV skipped (max_expert_rows) are left alone.
 template <bool GATED>
 __global__ void __launch_bounds__(256) qgemv_reduce_kernel(QgemvArgs a, int num_slots_e) {
   const int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -475,7 +474,7 @@ __global__ void __launch_bounds__(256) qgemv_reduce_kernel(QgemvArgs a, int num_
   if (a.offsets) {
     const int64_t valid = a.offsets[num_slots_e];
     if (pos >= valid) return;
-    if (a.max_expert_rows || a.min_expert_rows) {
+    if (a.max_expert_rows) {
       int l = 0, r = num_slots_e;  // expert e with offsets[e] <= pos < offsets[e + 1]
       while (r - l > 1) {
         const int m = (l + r) >> 1;
@@ -483,8 +482,7 @@ __global__ void __launch_bounds__(256) qgemv_reduce_kernel(QgemvArgs a, int num_
         else r = m;
       }
       const int64_t cnt = a.offsets[l + 1] - a.offsets[l];
-      if (a.max_expert_rows && cnt >= a.max_expert_rows) return;
-      if (a.min_expert_rows && cnt < a.min_expert_rows) return;
+      if (cnt >= a.max_expert_rows) return;
     }
   }
   const int N2 = GATED ? 2 * N : N;
