@@ -17,6 +17,17 @@
 
 namespace moe {
 
+// (a0, a1) = (fma(x.x, w, a0), fma(x.y, w, a1)) as one packed fp32x2 fma, round to
+// nearest even in each half.
+MOE_DEV void fma2_acc(float& a0, float& a1, float2 x, float w) {
+  unsigned long long acc, xx, ww;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(acc) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(xx) : "f"(x.x), "f"(x.y));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(ww) : "f"(w));
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(xx), "l"(ww));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(acc));
+}
+
 // Logits of rows row0 .. row0+NE-1 for tokens t0 .. t0+NT-1 (one warp).
 template <int NE, int NT>
 MOE_DEV void router_tile(const RouterArgs& a, int row0, int t0, int lane) {
@@ -79,12 +90,26 @@ MOE_DEV void router_tile(const RouterArgs& a, int row0, int t0, int lane) {
           const float q = __fsub_rn(__uint_as_float(((wd >> (4 * el)) & 0xfu) | 0x4b000000u), 8388608.0f);
           wq[e] = __fmaf_rn(sc[e], q, bi[e]);
         }
+        if (NT % 2 == 0) {
+          // two tokens per packed fp32x2 fma (two independent IEEE fmas, the same result
+          // as two scalar fmas)
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          const uint32_t xw = (el >> 1) == 0 ? xv[t].x : (el >> 1) == 1 ? xv[t].y : (el >> 1) == 2 ? xv[t].z : xv[t].w;
-          const float xe = (el & 1) ? bf_hi(xw) : bf_lo(xw);
+          for (int t = 0; t < NT; t += 2) {
+            const uint32_t xa = (el >> 1) == 0 ? xv[t].x : (el >> 1) == 1 ? xv[t].y : (el >> 1) == 2 ? xv[t].z : xv[t].w;
+            const uint32_t xb = (el >> 1) == 0 ? xv[t + 1].x : (el >> 1) == 1 ? xv[t + 1].y
+                              : (el >> 1) == 2 ? xv[t + 1].z : xv[t + 1].w;
+            const float2 xe = make_float2((el & 1) ? bf_hi(xa) : bf_lo(xa), (el & 1) ? bf_hi(xb) : bf_lo(xb));
 #pragma unroll
-          for (int e = 0; e < NE; ++e) acc[e][t] = __fmaf_rn(xe, wq[e], acc[e][t]);
+            for (int e = 0; e < NE; ++e) fma2_acc(acc[e][t], acc[e][t + 1], xe, wq[e]);
+          }
+        } else {
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            const uint32_t xw = (el >> 1) == 0 ? xv[t].x : (el >> 1) == 1 ? xv[t].y : (el >> 1) == 2 ? xv[t].z : xv[t].w;
+            const float xe = (el & 1) ? bf_hi(xw) : bf_lo(xw);
+#pragma unroll
+            for (int e = 0; e < NE; ++e) acc[e][t] = __fmaf_rn(xe, wq[e], acc[e][t]);
+          }
         }
       }
     }
