@@ -78,6 +78,9 @@ MOE_DEV uint2 lds_u2(uint32_t a) {
   asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "r"(a));
   return v;
 }
+MOE_DEV void sts_u2(uint32_t a, uint32_t x, uint32_t y) {
+  asm volatile("st.shared.v2.u32 [%0], {%1,%2};\n" ::"r"(a), "r"(x), "r"(y) : "memory");
+}
 MOE_DEV float2 lds_f2(uint32_t a) {
   float2 v;
   asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];\n" : "=f"(v.x), "=f"(v.y) : "r"(a));
@@ -85,6 +88,12 @@ MOE_DEV float2 lds_f2(uint32_t a) {
 }
 MOE_DEV void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src));
+}
+MOE_DEV void cp_async8(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst), "l"(src));
+}
+MOE_DEV void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(dst), "l"(src));
 }
 MOE_DEV void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>
@@ -109,17 +118,22 @@ struct RowMap {
 // Shared memory:
 //   xperm [kTok][(K + 8) bf16]   staged token rows in fragment order (16-byte row pad)
 //   xsum  [G][kTok] fp32         per-token sums of each group of 64
-//   rings [warps][NS][MT*16 rows][128 B]  weight chunks; the 32-byte group slot of
-//         ring row r is stored at slot (group ^ (r & 3)), which keeps the lanes' 8-byte
-//         fragment reads conflict-free.
+//   rings [warps][NS] stages of: [MT*16 rows][128 B] weight chunk; the 32-byte group
+//         slot of ring row r is stored at slot (group ^ (r & 3)), which keeps the lanes'
+//         8-byte fragment reads conflict-free; then [MT*16 rows][4] bf16 scales and
+//         [MT*16 rows][4] bf16 biases of the chunk's groups (copied with the weights, so
+//         no scale load is outstanding in registers across a chunk).
 template <bool GATED, int MT, int NC, int NS, bool SPLIT>
 __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_expert, int ctas_per_expert,
                                                     int max_slots) {
   constexpr int ROWS = GATED ? 8 * MT : 16 * MT;  // output rows per unit
   constexpr int TOK = kTok * NC;                  // tokens per pass over the weights
   constexpr int kRingRows = MT * 16;
-  constexpr int kStageBytes = kRingRows * kKC * 32;
+  constexpr int kSOff = kRingRows * kKC * 32;          // scales within a stage
+  constexpr int kBOff = kSOff + kRingRows * kKC * 2;     // biases within a stage
+  constexpr int kStageBytes = kBOff + kRingRows * kKC * 2;
   constexpr int kPieces = kRingRows * kKC * 2 / 32;  // 16-byte copies per lane per chunk
+  constexpr int kSPieces = (2 * kRingRows + 31) / 32;  // (row, scales|biases) copies per lane
   extern __shared__ __align__(16) unsigned char smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int gq = lane >> 2, cq = lane & 3;
@@ -192,14 +206,50 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
     for (int i = 0; i < kPieces; ++i) src[i] += (size_t)c_begin * kKC * 8;
   }
   int issued = 0;  // chunks issued so far in this token chunk
-  auto reset_src = [&]() {
-#pragma unroll
-    for (int i = 0; i < kPieces; ++i) src[i] -= (size_t)issued * kKC * 8;
-    issued = 0;
+  // Scales and biases travel with the weights into the stage: 8-byte cp.async when G % 4
+  // == 0 and the bases are 8-byte aligned, two 4-byte ones when G is even and they are
+  // 4-byte aligned, otherwise plain loads and shared stores at issue time (odd G, or no
+  // biases: zeros).
+  const uintptr_t align_bits = reinterpret_cast<uintptr_t>(a.s0) | reinterpret_cast<uintptr_t>(a.b0) |
+                               (GATED ? (reinterpret_cast<uintptr_t>(a.s1) | reinterpret_cast<uintptr_t>(a.b1)) : 0);
+  const bool has_b = a.b0 != nullptr && (!GATED || a.b1 != nullptr);
+  const bool s4 = has_b && (G & 1) == 0 && (align_bits & 3) == 0;
+  const bool s8 = s4 && (G & 3) == 0 && (align_bits & 7) == 0;
+  // ring row -> scale (which = 0) or bias (which = 1) row pointer
+  auto srow = [&](int rr, int which) -> const uint16_t* {
+    const int t = rr >> 4, r = rr & 15;
+    int row;
+    const uint16_t* S;
+    if (GATED) {
+      row = r0 + 8 * t + (r & 7);
+      S = (r < 8) ? (which ? a.b0 : a.s0) : (which ? a.b1 : a.s1);
+    } else {
+      row = r0 + 16 * t + r;
+      S = which ? a.b0 : a.s0;
+    }
+    row = row < N ? row : N - 1;
+    return S ? S + ((size_t)e * N + row) * G : nullptr;
   };
+  const uint16_t* ssrc[kSPieces];
+  uint32_t sdst[kSPieces];
+  bool sval[kSPieces];
+#pragma unroll
+  for (int i = 0; i < kSPieces; ++i) {
+    const int q = i * 32 + lane;
+    sval[i] = q < 2 * kRingRows;
+    const int rr = q % kRingRows, which = q / kRingRows;
+    ssrc[i] = sval[i] ? srow(rr, which) : nullptr;  // null: no biases
+    sdst[i] = (which ? kBOff : kSOff) + rr * (kKC * 2);
+  }
+  if (SPLIT) {
+#pragma unroll
+    for (int i = 0; i < kSPieces; ++i)
+      if (ssrc[i]) ssrc[i] += (size_t)c_begin * kKC;
+  }
   auto issue_chunk = [&](int c) {
     const uint32_t st = ring_s + (uint32_t)((c % NS) * kStageBytes);
-    if (c + 1 < nchunks || tail_groups == kKC) {
+    const bool full = c + 1 < nchunks || tail_groups == kKC;
+    if (full) {
 #pragma unroll
       for (int i = 0; i < kPieces; ++i) cp_async16(st + dst[i], src[i]);
     } else {
@@ -209,36 +259,35 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
     }
 #pragma unroll
     for (int i = 0; i < kPieces; ++i) src[i] += kKC * 8;
+#pragma unroll
+    for (int i = 0; i < kSPieces; ++i) {
+      if (sval[i]) {
+        if (s8) {
+          cp_async8(st + sdst[i], ssrc[i]);
+        } else if (s4) {
+          cp_async4(st + sdst[i], ssrc[i]);  // groups 0-1 of the chunk (G is even)
+          if (full) cp_async4(st + sdst[i] + 4, ssrc[i] + 2);
+        } else {
+          uint16_t v[kKC];
+#pragma unroll
+          for (int q = 0; q < kKC; ++q) v[q] = (ssrc[i] && c * kKC + q < G) ? ssrc[i][q] : (uint16_t)0;
+          sts_u2(st + sdst[i], v[0] | ((uint32_t)v[1] << 16), v[2] | ((uint32_t)v[3] << 16));
+        }
+        if (ssrc[i]) ssrc[i] += kKC;
+      }
+    }
     ++issued;
     cp_commit();
   };
 
-  // lane's scale rows per tile: lo = MMA row gq, hi = MMA row gq + 8
-  const uint16_t* sp[MT][2];
-  const uint16_t* bp[MT][2];
+  auto reset_src = [&]() {
 #pragma unroll
-  for (int t = 0; t < MT; ++t)
+    for (int i = 0; i < kPieces; ++i) src[i] -= (size_t)issued * kKC * 8;
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      int row;
-      const uint16_t *S, *B;
-      if (GATED) {
-        row = r0 + 8 * t + gq;
-        S = h ? a.s1 : a.s0;
-        B = h ? a.b1 : a.b0;
-      } else {
-        row = r0 + 16 * t + gq + 8 * h;
-        S = a.s0;
-        B = a.b0;
-      }
-      row = row < N ? row : N - 1;
-      const size_t off = ((size_t)e * N + row) * G;
-      sp[t][h] = S + off;
-      bp[t][h] = B ? B + off : nullptr;
-    }
-  const uintptr_t align_bits = reinterpret_cast<uintptr_t>(a.s0) | reinterpret_cast<uintptr_t>(a.b0) |
-                               (GATED ? (reinterpret_cast<uintptr_t>(a.s1) | reinterpret_cast<uintptr_t>(a.b1)) : 0);
-  const bool vec_scales = (G & 3) == 0 && (align_bits & 7) == 0;
+    for (int i = 0; i < kSPieces; ++i)
+      if (ssrc[i]) ssrc[i] -= (size_t)issued * kKC;
+    issued = 0;
+  };
 
   for (int64_t cbase = row_begin; cbase < row_end; cbase += TOK) {
     const int ntok = (row_end - cbase < TOK) ? (int)(row_end - cbase) : TOK;
@@ -306,42 +355,23 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
 #pragma unroll
         for (int q = 0; q < 4; ++q) acc[n][t][q] = 0.0f;
 
-    // scales of the lane's rows, (s, b) for kKC groups, loaded one chunk ahead
-    uint32_t sw[MT][2][2], bw[MT][2][2];  // [tile][lo/hi][pair of groups]
-    auto load_scales = [&](int c, uint32_t (&sv2)[MT][2][2], uint32_t (&bv2)[MT][2][2]) {
-      const int g0 = c * kKC;
-#pragma unroll
-      for (int t = 0; t < MT; ++t)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (vec_scales) {
-            const uint2 s2 = *reinterpret_cast<const uint2*>(sp[t][h] + g0);
-            const uint2 b2 = bp[t][h] ? *reinterpret_cast<const uint2*>(bp[t][h] + g0) : make_uint2(0, 0);
-            sv2[t][h][0] = s2.x; sv2[t][h][1] = s2.y;
-            bv2[t][h][0] = b2.x; bv2[t][h][1] = b2.y;
-          } else {
-            uint16_t sv[kKC], bv[kKC];
-#pragma unroll
-            for (int i = 0; i < kKC; ++i) {
-              const bool in = g0 + i < G;
-              sv[i] = in ? sp[t][h][g0 + i] : 0;
-              bv[i] = (in && bp[t][h]) ? bp[t][h][g0 + i] : 0;
-            }
-            sv2[t][h][0] = sv[0] | ((uint32_t)sv[1] << 16); sv2[t][h][1] = sv[2] | ((uint32_t)sv[3] << 16);
-            bv2[t][h][0] = bv[0] | ((uint32_t)bv[1] << 16); bv2[t][h][1] = bv[2] | ((uint32_t)bv[3] << 16);
-          }
-        }
-    };
-    load_scales(c_begin, sw, bw);
     for (int c = c_begin; c < c_end; ++c) {
       if (c + NS - 1 < c_end) issue_chunk(c + NS - 1);
       else cp_commit();
-      uint32_t swn[MT][2][2], bwn[MT][2][2];
-      if (c + 1 < c_end) load_scales(c + 1, swn, bwn);
       const int g0 = c * kKC;
       cp_wait<NS - 1>();
       __syncwarp();
       const uint32_t st = ring_s + (uint32_t)((c % NS) * kStageBytes);
+      // this chunk's scales and biases of the lane's rows: [tile][lo/hi] = 4 bf16 (groups)
+      uint2 sw[MT][2], bw[MT][2];
+#pragma unroll
+      for (int t = 0; t < MT; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int rr = t * 16 + gq + 8 * h;
+          sw[t][h] = lds_u2(st + kSOff + rr * (kKC * 2));
+          bw[t][h] = lds_u2(st + kBOff + rr * (kKC * 2));
+        }
 #pragma unroll
       for (int gl = 0; gl < kKC; ++gl) {
         const int g = g0 + gl;
@@ -373,8 +403,10 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
                 else mma_acc(d[n], a0, a1, a2, a3, bfr[n][2 * j], bfr[n][2 * j + 1]);
               }
             }
-            const uint32_t s_lo2 = sw[t][0][gl >> 1], s_hi2 = sw[t][1][gl >> 1];
-            const uint32_t b_lo2 = bw[t][0][gl >> 1], b_hi2 = bw[t][1][gl >> 1];
+            const uint32_t s_lo2 = (gl >> 1) ? sw[t][0].y : sw[t][0].x;
+            const uint32_t s_hi2 = (gl >> 1) ? sw[t][1].y : sw[t][1].x;
+            const uint32_t b_lo2 = (gl >> 1) ? bw[t][0].y : bw[t][0].x;
+            const uint32_t b_hi2 = (gl >> 1) ? bw[t][1].y : bw[t][1].x;
             const float s_l = (gl & 1) ? bf_hi(s_lo2) : bf_lo(s_lo2);
             const float s_h = (gl & 1) ? bf_hi(s_hi2) : bf_lo(s_hi2);
             const float c_l = __fmaf_rn(-128.0f, s_l, (gl & 1) ? bf_hi(b_lo2) : bf_lo(b_lo2));
@@ -390,17 +422,6 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
         }
       }
       __syncwarp();  // every lane is done with this stage before it is refilled
-      if (c + 1 < c_end) {
-#pragma unroll
-        for (int t = 0; t < MT; ++t)
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-              sw[t][h][q] = swn[t][h][q];
-              bw[t][h][q] = bwn[t][h][q];
-            }
-      }
     }
     cp_wait<0>();
     pdl_trigger();
@@ -503,7 +524,7 @@ static cudaError_t launch_split_t(const QgemvArgs& a, int upe, int cpe, int slot
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   const int G = a.K / 64;
   const size_t smem = (size_t)kTok * NC * (2 * a.K + 16) + (size_t)G * kTok * NC * 4 +
-                      (size_t)wpc * NS * MT * 16 * kKC * 32;
+                      (size_t)wpc * NS * MT * 16 * (kKC * 32 + kKC * 4);  // weights + scales + biases
   if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
   auto kern = qgemv_kernel<GATED, MT, NC, NS, SPLIT>;
   static thread_local int set_dev = -1;
