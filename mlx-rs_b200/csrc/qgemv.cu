@@ -101,6 +101,9 @@ MOE_DEV void cp_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
+// Piece swizzle of the whole-K scale regions (16-byte pieces within a row).
+MOE_DEV int fk_swz(int r, int G) { return (G & 31) == 0 ? ((r >> 1) & 3) : 0; }
+
 struct RowMap {
   int x_mode, x_repeat;
   const uint32_t* lhs;
@@ -123,15 +126,21 @@ struct RowMap {
 //         8-byte fragment reads conflict-free; then [MT*16 rows][4] bf16 scales and
 //         [MT*16 rows][4] bf16 biases of the chunk's groups (copied with the weights, so
 //         no scale load is outstanding in registers across a chunk).
-template <bool GATED, int MT, int NC, int NS, bool SPLIT>
-__global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_expert, int ctas_per_expert,
-                                                    int max_slots) {
+// FK (whole-K scales, 16-warp CTAs): the stages hold weights only; each warp's scales
+// and biases for all of K sit in one region per warp, copied once per launch with
+// coalesced 16-byte cp.async (the unit's rows are contiguous in the MLX layout), so
+// every 32-byte sector of the scale arrays is fetched once instead of once per chunk:
+//   sregion [warps][s: ring rows][G] bf16, [b: ring rows][G] bf16 (gated: the MT*8 gate
+//           rows, then the MT*8 up rows), between xsum and the rings.
+template <bool GATED, int MT, int NC, int NS, bool SPLIT, bool FK = false>
+__global__ void __launch_bounds__(FK ? 512 : 256) qgemv_kernel(QgemvArgs a, int units_per_expert,
+                                                               int ctas_per_expert, int max_slots) {
   constexpr int ROWS = GATED ? 8 * MT : 16 * MT;  // output rows per unit
   constexpr int TOK = kTok * NC;                  // tokens per pass over the weights
   constexpr int kRingRows = MT * 16;
   constexpr int kSOff = kRingRows * kKC * 32;          // scales within a stage
   constexpr int kBOff = kSOff + kRingRows * kKC * 2;     // biases within a stage
-  constexpr int kStageBytes = kBOff + kRingRows * kKC * 2;
+  constexpr int kStageBytes = FK ? kSOff : kBOff + kRingRows * kKC * 2;
   constexpr int kPieces = kRingRows * kKC * 2 / 32;  // 16-byte copies per lane per chunk
   constexpr int kSPieces = (2 * kRingRows + 31) / 32;  // (row, scales|biases) copies per lane
   extern __shared__ __align__(16) unsigned char smem[];
@@ -161,7 +170,10 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
   const uint32_t xperm_s = smem_s;
   const uint32_t xsum_s = xperm_s + TOK * xrow_bytes;
   float* xsum = reinterpret_cast<float*>(smem + TOK * xrow_bytes);
-  const uint32_t ring_s = xsum_s + G * TOK * 4 + warp * NS * kStageBytes;
+  const uint32_t sreg_all = xsum_s + G * TOK * 4;                 // FK scale regions
+  const uint32_t sreg_s = sreg_all + (uint32_t)(warp * kRingRows * G * 4);
+  const uint32_t ring_s = sreg_all + (FK ? (uint32_t)(nwarps * kRingRows * G * 4) : 0u) +
+                          (uint32_t)(warp * NS * kStageBytes);
 
   // ring row -> global weight row (clamped into the matrix: rows past N compute junk
   // that is never stored)
@@ -236,7 +248,7 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
 #pragma unroll
   for (int i = 0; i < kSPieces; ++i) {
     const int q = i * 32 + lane;
-    sval[i] = q < 2 * kRingRows;
+    sval[i] = !FK && q < 2 * kRingRows;
     const int rr = q % kRingRows, which = q / kRingRows;
     ssrc[i] = sval[i] ? srow(rr, which) : nullptr;  // null: no biases
     sdst[i] = (which ? kBOff : kSOff) + rr * (kKC * 2);
@@ -289,6 +301,28 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
     issued = 0;
   };
 
+  if (FK && unit_live) {
+    // the unit's scale and bias rows for all of K: 2 (gated: 4) contiguous regions of
+    // the MLX arrays; part of the first chunk's copy group
+    // 16-byte piece p of region row r lands at piece p ^ fk_swz(r): with 64-byte rows
+    // (G = 32) the lanes' 8-byte reads of 8 rows then fall in distinct banks
+    constexpr int kRegions = GATED ? 4 : 2;
+    const int rrows = GATED ? MT * 8 : MT * 16;
+    const int rbytes = rrows * G * 2;
+    const int npieces = G / 8;
+#pragma unroll
+    for (int rg = 0; rg < kRegions; ++rg) {
+      const uint16_t* base = GATED ? (rg == 0 ? a.s0 : rg == 1 ? a.s1 : rg == 2 ? a.b0 : a.b1)
+                                   : (rg == 0 ? a.s0 : a.b0);
+      const unsigned char* srcb =
+          reinterpret_cast<const unsigned char*>(base + ((size_t)e * N + r0) * G);
+      const uint32_t dstb = sreg_s + (uint32_t)(rg * rbytes);
+      for (int idx = lane; idx < rrows * npieces; idx += 32) {
+        const int r = idx / npieces, pc = idx - r * npieces;
+        cp_async16(dstb + r * G * 2 + ((pc ^ fk_swz(r, G)) << 4), srcb + r * G * 2 + (pc << 4));
+      }
+    }
+  }
   for (int64_t cbase = row_begin; cbase < row_end; cbase += TOK) {
     const int ntok = (row_end - cbase < TOK) ? (int)(row_end - cbase) : TOK;
     reset_src();
@@ -368,9 +402,20 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QgemvArgs a, int units_per_e
       for (int t = 0; t < MT; ++t)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int rr = t * 16 + gq + 8 * h;
-          sw[t][h] = lds_u2(st + kSOff + rr * (kKC * 2));
-          bw[t][h] = lds_u2(st + kBOff + rr * (kKC * 2));
+          if (FK) {
+            // region row: gated h = 0 gate row 8t+gq, h = 1 up row 8t+gq (second region);
+            // plain rows 16t+gq (+8)
+            const int r = GATED ? t * 8 + gq : t * 16 + gq + 8 * h;  // row within its region
+            const int fr = GATED ? h * (MT * 8) + r : r;
+            const uint32_t so =
+                sreg_s + (uint32_t)(fr * G * 2 + ((((g0 >> 3) ^ fk_swz(r, G))) << 4) + (g0 & 7) * 2);
+            sw[t][h] = lds_u2(so);
+            bw[t][h] = lds_u2(so + kRingRows * G * 2);
+          } else {
+            const int rr = t * 16 + gq + 8 * h;
+            sw[t][h] = lds_u2(st + kSOff + rr * (kKC * 2));
+            bw[t][h] = lds_u2(st + kBOff + rr * (kKC * 2));
+          }
         }
 #pragma unroll
       for (int gl = 0; gl < kKC; ++gl) {
@@ -518,15 +563,21 @@ __global__ void __launch_bounds__(256) qgemv_reduce_kernel(QgemvArgs a, int num_
   a.out[(size_t)orow * N + n] = GATED ? swiglu_bf16(rbf(g), rbf(u)) : f2bf(g);
 }
 
-template <bool GATED, int MT, int NC, int NS, bool SPLIT>
+template <int MT, int NC, int NS, bool FK>
+static size_t qgemv_smem(int K, int wpc) {
+  const int G = K / 64;
+  return (size_t)kTok * NC * (2 * K + 16) + (size_t)G * kTok * NC * 4 +
+         (FK ? (size_t)wpc * MT * 16 * G * 4 + (size_t)wpc * NS * MT * 16 * kKC * 32
+             : (size_t)wpc * NS * MT * 16 * (kKC * 32 + kKC * 4));  // weights (+ scales + biases)
+}
+
+template <bool GATED, int MT, int NC, int NS, bool SPLIT, bool FK = false>
 static cudaError_t launch_split_t(const QgemvArgs& a, int upe, int cpe, int slots, int wpc, cudaStream_t st) {
   const long long blocks = (long long)cpe * slots * a.ksplit;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  const int G = a.K / 64;
-  const size_t smem = (size_t)kTok * NC * (2 * a.K + 16) + (size_t)G * kTok * NC * 4 +
-                      (size_t)wpc * NS * MT * 16 * (kKC * 32 + kKC * 4);  // weights + scales + biases
+  const size_t smem = qgemv_smem<MT, NC, NS, FK>(a.K, wpc);
   if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
-  auto kern = qgemv_kernel<GATED, MT, NC, NS, SPLIT>;
+  auto kern = qgemv_kernel<GATED, MT, NC, NS, SPLIT, FK>;
   static thread_local int set_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -538,7 +589,7 @@ static cudaError_t launch_split_t(const QgemvArgs& a, int upe, int cpe, int slot
   return launch_k(kern, dim3((unsigned)blocks), dim3(wpc * 32), smem, st, a, upe, cpe, slots);
 }
 
-template <bool GATED, int MT, int NC, int NS>
+template <bool GATED, int MT, int NC, int NS, bool FK = false>
 static cudaError_t launch_qgemv_t(const QgemvArgs& a0, int slots, int wpc, cudaStream_t st) {
   constexpr int ROWS = GATED ? 8 * MT : 16 * MT;
   QgemvArgs a = a0;
@@ -564,6 +615,10 @@ static cudaError_t launch_qgemv_t(const QgemvArgs& a0, int slots, int wpc, cudaS
       if (ks > 1 && need <= a.partial_bytes) a.ksplit = ks;
     }
   }
+  if (FK) {  // chosen only for grids that fill the GPU, which are never split
+    a.ksplit = 1;
+    return launch_split_t<GATED, MT, NC, NS, false, FK>(a, upe, cpe, slots, wpc, st);
+  }
   cudaError_t err = a.ksplit > 1 ? launch_split_t<GATED, MT, NC, NS, true>(a, upe, cpe, slots, wpc, st)
                                   : launch_split_t<GATED, MT, NC, NS, false>(a, upe, cpe, slots, wpc, st);
   if (err != cudaSuccess || a.ksplit == 1) return err;
@@ -580,8 +635,25 @@ cudaError_t launch_gemv_reduce(const QgemvArgs& a, bool gated, cudaStream_t st) 
                : launch_k(qgemv_reduce_kernel<false>, grid, dim3(256), 0, st, a, a.num_experts_total);
 }
 
+// Whole-K scales in 16-warp CTAs (one per SM) for the wide one-token-chunk case: needs
+// the unit's scale rows whole and 16-byte aligned and the shared memory.
+static bool use_fk(const QgemvArgs& a, bool gated) {
+  const int G = a.K / 64;
+  const int rows = gated ? 16 : 32;  // rows of one unit (MT = 2)
+  const uintptr_t al = reinterpret_cast<uintptr_t>(a.s0) | reinterpret_cast<uintptr_t>(a.b0) |
+                       (gated ? reinterpret_cast<uintptr_t>(a.s1) | reinterpret_cast<uintptr_t>(a.b1) : 0);
+  // 16-byte row pieces (G % 8 == 0); worth it from 6 chunks of K on (measured: K = 2048
+  // gains 9%, K = 768 loses 6% against per-chunk scales)
+  if (!a.b0 || (gated && !a.b1) || (al & 15) || (G & 7) || G < 24 || (a.N % rows)) return false;
+  if (((size_t)a.N * G * 2) % 16) return false;  // expert stride of the scale arrays
+  const char* env = std::getenv("MOE_B200_GEMV_FK");  // "0": per-chunk scales only
+  if (env && env[0] == '0') return false;
+  return qgemv_smem<2, 1, 2, true>(a.K, 16) <= 227 * 1024;
+}
+
 template <bool GATED, int NC>
 static cudaError_t launch_qgemv_nc(const QgemvArgs& a, int slots, bool wide, cudaStream_t st) {
+  if (NC == 1 && wide && use_fk(a, GATED)) return launch_qgemv_t<GATED, 2, 1, 2, true>(a, slots, 16, st);
   return wide ? launch_qgemv_t<GATED, 2, NC, 2>(a, slots, 8, st) : launch_qgemv_t<GATED, 1, NC, 4>(a, slots, 4, st);
 }
 

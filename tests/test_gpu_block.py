@@ -317,3 +317,24 @@ def test_split_k_gemv_matches_unsplit_and_oracle(cfg_name, seed, T, monkeypatch)
     assert_close(got[0].reshape(T, -1), ref[0].reshape(T, -1), f"{cfg_name} split vs unsplit", ULP_TOL)
     y, _, _ = O.block_forward(bw, x)
     assert_close(got[0].reshape(T, -1), y, f"{cfg_name} split vs oracle", ULP_TOL)
+
+
+@pytest.mark.parametrize("cfg_name,seed,T", [("QWEN3_30B_A3B", 1, 64), ("LFM2_8B_A1B", 3, 32),
+                                              ("QWEN15_MOE_A27B", 2, 48)])
+def test_whole_k_scale_gemv_bit_identical(cfg_name, seed, T, monkeypatch):
+    """The decode GEMV with each unit's scales for all of K copied once (16-warp CTAs)
+    computes exactly what the per-chunk scale copies compute: same bits, and the oracle
+    within tolerance."""
+    import oracle as O
+    from gpu_util import run_block
+    cfg = getattr(S, cfg_name)
+    bw, blk = _block(cfg, seed)
+    x = S.host_x(700 + T, T, cfg.hidden)
+    monkeypatch.setenv("MOE_B200_GEMV_FK", "0")
+    ref = run_block(blk, x)
+    monkeypatch.setenv("MOE_B200_GEMV_FK", "1")
+    got = run_block(blk, x)
+    for u, v in zip(got, ref):
+        assert np.array_equal(u, v)
+    y, _, _ = O.block_forward(bw, x)
+    assert_close(got[0].reshape(T, -1), y, f"{cfg_name} whole-K scales vs oracle", ULP_TOL)
