@@ -305,7 +305,9 @@ __global__ void __launch_bounds__(FK ? 512 : 256) qgemv_kernel(QgemvArgs a, int 
     // the unit's scale and bias rows for all of K: 2 (gated: 4) contiguous regions of
     // the MLX arrays; part of the first chunk's copy group
     // 16-byte piece p of region row r lands at piece p ^ fk_swz(r): with 64-byte rows
-    // (G = 32) the lanes' 8-byte reads of 8 rows then fall in distinct banks
+    // (G = 32) the lanes' 8-byte reads of 8 rows then fall in distinct banks; other G
+    // (rows of 24, 48, 56, 80 ... bytes) are conflict-free as they are and the region is
+    // copied flat
     constexpr int kRegions = GATED ? 4 : 2;
     const int rrows = GATED ? MT * 8 : MT * 16;
     const int rbytes = rrows * G * 2;
@@ -317,9 +319,13 @@ __global__ void __launch_bounds__(FK ? 512 : 256) qgemv_kernel(QgemvArgs a, int 
       const unsigned char* srcb =
           reinterpret_cast<const unsigned char*>(base + ((size_t)e * N + r0) * G);
       const uint32_t dstb = sreg_s + (uint32_t)(rg * rbytes);
-      for (int idx = lane; idx < rrows * npieces; idx += 32) {
-        const int r = idx / npieces, pc = idx - r * npieces;
-        cp_async16(dstb + r * G * 2 + ((pc ^ fk_swz(r, G)) << 4), srcb + r * G * 2 + (pc << 4));
+      if ((G & 31) == 0) {
+        for (int idx = lane; idx < rrows * npieces; idx += 32) {
+          const int r = idx / npieces, pc = idx - r * npieces;
+          cp_async16(dstb + r * G * 2 + ((pc ^ fk_swz(r, G)) << 4), srcb + r * G * 2 + (pc << 4));
+        }
+      } else {
+        for (int off = lane * 16; off < rbytes; off += 32 * 16) cp_async16(dstb + off, srcb + off);
       }
     }
   }
@@ -635,25 +641,32 @@ cudaError_t launch_gemv_reduce(const QgemvArgs& a, bool gated, cudaStream_t st) 
                : launch_k(qgemv_reduce_kernel<false>, grid, dim3(256), 0, st, a, a.num_experts_total);
 }
 
-// Whole-K scales in 16-warp CTAs (one per SM) for the wide one-token-chunk case: needs
-// the unit's scale rows whole and 16-byte aligned and the shared memory.
-static bool use_fk(const QgemvArgs& a, bool gated) {
+// Whole-K scales for the wide one-token-chunk case: warps per CTA (16 or 8) or 0 when
+// not used. Needs the unit's scale rows whole, 16-byte aligned regions and 8-byte
+// aligned chunk scales (G % 4 == 0). Long K (G >= 24, G % 8 == 0: 16-byte rows) runs
+// 16-warp CTAs, whose one staging of x serves twice the rows and leaves room for the
+// scales; shorter K keeps 8-warp CTAs, two per SM (measured: K = 2048 in 16-warp CTAs
+// gains 9% and K = 768 loses 6% against per-chunk scale copies).
+static int fk_warps(const QgemvArgs& a, bool gated) {
   const int G = a.K / 64;
   const int rows = gated ? 16 : 32;  // rows of one unit (MT = 2)
   const uintptr_t al = reinterpret_cast<uintptr_t>(a.s0) | reinterpret_cast<uintptr_t>(a.b0) |
                        (gated ? reinterpret_cast<uintptr_t>(a.s1) | reinterpret_cast<uintptr_t>(a.b1) : 0);
-  // 16-byte row pieces (G % 8 == 0); worth it from 6 chunks of K on (measured: K = 2048
-  // gains 9%, K = 768 loses 6% against per-chunk scales)
-  if (!a.b0 || (gated && !a.b1) || (al & 15) || (G & 7) || G < 24 || (a.N % rows)) return false;
-  if (((size_t)a.N * G * 2) % 16) return false;  // expert stride of the scale arrays
+  if (!a.b0 || (gated && !a.b1) || (al & 15) || (G & 3) || (a.N % rows)) return 0;
+  if (((size_t)a.N * G * 2) % 16) return 0;  // expert stride of the scale arrays
   const char* env = std::getenv("MOE_B200_GEMV_FK");  // "0": per-chunk scales only
-  if (env && env[0] == '0') return false;
-  return qgemv_smem<2, 1, 2, true>(a.K, 16) <= 227 * 1024;
+  if (env && env[0] == '0') return 0;
+  if (G >= 24 && (G & 7) == 0 && qgemv_smem<2, 1, 2, true>(a.K, 16) <= 227 * 1024) return 16;
+  if (G < 24 && 2 * (qgemv_smem<2, 1, 2, true>(a.K, 8) + 1024) <= 228 * 1024) return 8;
+  return 0;
 }
 
 template <bool GATED, int NC>
 static cudaError_t launch_qgemv_nc(const QgemvArgs& a, int slots, bool wide, cudaStream_t st) {
-  if (NC == 1 && wide && use_fk(a, GATED)) return launch_qgemv_t<GATED, 2, 1, 2, true>(a, slots, 16, st);
+  if (NC == 1 && wide) {
+    const int fw = fk_warps(a, GATED);
+    if (fw) return launch_qgemv_t<GATED, 2, 1, 2, true>(a, slots, fw, st);
+  }
   return wide ? launch_qgemv_t<GATED, 2, NC, 2>(a, slots, 8, st) : launch_qgemv_t<GATED, 1, NC, 4>(a, slots, 4, st);
 }
 
