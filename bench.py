@@ -144,8 +144,8 @@ class ClockSampler:
 # DRAM traffic per launch of the dominant kernel (dram__bytes_read.sum +
 # dram__bytes_write.sum) from one ncu --set full capture of the same workload on a B200.
 NCU_TRAFFIC = {
-    ("decode", "gate_up"): 216_633_856 + 4_721_408,
-    ("decode", "down"): 107_877_376 + 4_674_304,
+    ("decode", "gate_up"): 215_520_768 + 4_102_656,
+    ("decode", "down"): 107_880_960 + 3_843_840,
     ("prefill", "gate_up"): 262_024_704 + 40_618_240,
     ("prefill", "down"): 163_624_704 + 99_390_976,
 }
