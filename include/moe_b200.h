@@ -160,6 +160,19 @@ int moe_block_forward(moe_ctx* ctx, const moe_block_config* cfg, const moe_block
                       const void* x, int64_t T, void* out);
 
 /*
+ * The MoE half of a decoder layer: out[T, H] = x + MoE(RMSNorm(x; norm_weight, eps)),
+ * the RMSNorm as moe_fast_rms_norm and the residual add fused into the combine
+ * (out = bf16(x + bf16(moe)), the bf16 add of the reference). Replaces the FFN half of
+ * MoeBlock::forward (qwen3_moe_python_port.rs:736-739: post_attention_layernorm,
+ * ff.forward, residual.add) and of Lfm2Layer::forward (lfm2_moe_python_port.rs:856-868:
+ * ffn_norm, ffn.forward, residual.add). normed[T, H] (optional) receives the RMSNorm
+ * output; NULL keeps it in the context's scratch. x, normed and out must not overlap.
+ */
+int moe_layer_ffn_forward(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts,
+                          const void* x, int64_t T, const void* norm_weight, float eps, void* normed,
+                          void* out);
+
+/*
  * Routing only (R1-R4 plus the per-expert grouping gather_qmm forms internally):
  *   idx[T, k] uint32      selected experts, by (score desc, index asc);
  *   weights[T, k] bf16    combine weights (renormalised when norm_topk_prob);

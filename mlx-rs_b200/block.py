@@ -96,6 +96,29 @@ class _Block:
 
     __call__ = forward
 
+    def forward_layer(self, x: torch.Tensor, norm_weight: torch.Tensor, eps: float = 1e-6,
+                      out: Optional[torch.Tensor] = None, normed: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """The MoE half of a decoder layer, x + block(RmsNorm(x)), with the residual add
+        fused into the combine (moe_layer_ffn_forward): post_attention_layernorm /
+        ff.forward / residual.add of MoeBlock::forward (qwen3_moe_python_port.rs:736-739),
+        ffn_norm / ffn.forward / residual.add of Lfm2Layer::forward
+        (lfm2_moe_python_port.rs:856-868)."""
+        H = self.config.hidden
+        fn = "moe_layer_ffn_forward"
+        if x.shape[-1] != H or x.dtype != torch.bfloat16 or not x.is_contiguous():
+            raise MlxError(fn, 1, "x must be contiguous bf16 [..., hidden]")
+        if norm_weight.dtype != torch.bfloat16 or norm_weight.numel() != H or not norm_weight.is_contiguous():
+            raise MlxError(fn, 1, "norm_weight must be contiguous bf16 [hidden]")
+        T = x.numel() // H
+        if out is None:
+            out = torch.empty_like(x)
+        ctx = _ctx(x)
+        rc = library().moe_layer_ffn_forward(ctx.handle, C.byref(self._cfg), C.byref(self._wts), _ptr(x), T,
+                                             _ptr(norm_weight), float(eps),
+                                             _ptr(normed) if normed is not None else None, _ptr(out))
+        ctx.check(fn, rc)
+        return out
+
     def profile(self, x: torch.Tensor, out: Optional[torch.Tensor] = None):
         """Run the block once with CUDA events between stages (synchronising).
         Returns (out, {stage: ms}, n_active_experts)."""
@@ -159,14 +182,22 @@ class RmsNorm:
 
 
 class MoeStack:
-    """h = x; for each layer l: if l > 0: h = RmsNorm_l(h); h = block_l(h)."""
+    """h = x; for each layer l: if l > 0: h = RmsNorm_l(h); h = block_l(h).
+    With ``residual=True`` the decoder layers' FFN halves instead:
+    h = h + block_l(RmsNorm_l(h)) for every l (one moe_layer_ffn_forward per layer)."""
 
-    def __init__(self, blocks: Sequence[_Block], norms: Sequence[RmsNorm]):
-        self.blocks, self.norms = list(blocks), list(norms)
+    def __init__(self, blocks: Sequence[_Block], norms: Sequence[RmsNorm], residual: bool = False):
+        self.blocks, self.norms, self.residual = list(blocks), list(norms), residual
+        if residual and any(n is None for n in self.norms):
+            raise ValueError("a residual stack needs a norm for every layer")
 
     def forward(self, x):
         h = x
         for l, blk in enumerate(self.blocks):
+            if self.residual:
+                n = self.norms[l]
+                h = blk.forward_layer(h, n.weight, n.eps)
+                continue
             if l > 0:
                 h = self.norms[l](h)
             h = blk(h)

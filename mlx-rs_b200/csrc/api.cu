@@ -132,6 +132,7 @@ struct BlockWs {
   size_t gemv_partial_bytes;
   float* tc_partial;    // split-K partials of the shared expert's tcgen05 GEMMs
   size_t tc_partial_bytes;
+  uint16_t* xnorm;      // RMSNorm(x) of the decoder-layer step
   size_t bytes;
 };
 
@@ -195,6 +196,7 @@ BlockWs carve_block(void* base, const moe_block_config* c, int64_t T) {
   const size_t ntc = tc_partial_floats(c, T);
   w.tc_partial = ntc ? cv.take<float>(ntc) : nullptr;
   w.tc_partial_bytes = ntc * sizeof(float);
+  w.xnorm = cv.take<uint16_t>(T * c->hidden);
   w.bytes = cv.off + 256;
   return w;
 }
@@ -493,7 +495,7 @@ moe::QgemvArgs qgemv_args(const moe_qweight& m0, const moe_qweight* m1, int N, i
 namespace {
 
 int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x, int64_t T,
-              void* out, cudaEvent_t* ev) {
+              void* out, cudaEvent_t* ev, const void* residual = nullptr) {
   if (!ctx) return MOE_ERR_INVALID;
   ctx->last_error.clear();
   const char* fn = "moe_block_forward";
@@ -619,6 +621,7 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   ca.weights = ws.wsel;
   ca.shared = shared ? ws.ys : nullptr;
   ca.gate_val = (shared && cfg->has_shared_gate) ? ws.gate_val : nullptr;
+  ca.residual = static_cast<const uint16_t*>(residual);
   ca.T = (int)T;
   ca.k = k;
   ca.H = H;
@@ -810,6 +813,39 @@ int moe_block_route(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_w
 int moe_block_forward(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x,
                       int64_t T, void* out) {
   return run_block(ctx, cfg, wts, x, T, out, nullptr);
+}
+
+int moe_layer_ffn_forward(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts,
+                          const void* x, int64_t T, const void* norm_weight, float eps, void* normed,
+                          void* out) {
+  if (!ctx) return MOE_ERR_INVALID;
+  ctx->last_error.clear();
+  const char* fn = "moe_layer_ffn_forward";
+  int rc = check_block(ctx, cfg, wts, fn);
+  if (rc) return rc;
+  if (T < 0 || T > (INT32_MAX / 64)) return fail(ctx, MOE_ERR_INVALID, "%s: bad T", fn);
+  if (T == 0) return MOE_OK;
+  if (!x || !out || !norm_weight || !aligned16(x) || !aligned16(out) || !aligned16(norm_weight) ||
+      (normed && !aligned16(normed)))
+    return fail(ctx, MOE_ERR_INVALID, "%s: x, norm_weight, out (and normed) must be non-null and 16-byte aligned",
+                fn);
+  const size_t row_bytes = (size_t)T * cfg->hidden * 2;
+  auto overlaps = [](const void* a, const void* b, size_t n) {
+    const char* p = static_cast<const char*>(a);
+    const char* q = static_cast<const char*>(b);
+    return p < q + n && q < p + n;
+  };
+  if (overlaps(x, out, row_bytes) || (normed && (overlaps(normed, out, row_bytes) || overlaps(normed, x, row_bytes))))
+    return fail(ctx, MOE_ERR_INVALID, "%s: x, normed and out must not overlap", fn);
+  if (!(eps >= 0.0f)) return fail(ctx, MOE_ERR_INVALID, "%s: eps must be >= 0", fn);
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  rc = ensure_scratch(ctx, carve_block(nullptr, cfg, T).bytes);
+  if (rc) return rc;
+  uint16_t* h = normed ? static_cast<uint16_t*>(normed) : carve_block(ctx->scratch, cfg, T).xnorm;
+  MOE_CUDA(ctx, moe::launch_rms_norm(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(norm_weight),
+                                     eps, T, cfg->hidden, h, ctx->stream));
+  return run_block(ctx, cfg, wts, h, T, out, nullptr, x);
 }
 
 int moe_block_profile(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x,

@@ -4,6 +4,9 @@
 // index order (expert_out.multiply(score).sum_axis(1), qwen3_moe_python_port.rs:471-472;
 // lfm2_moe_python_port.rs:718-732), then, with a shared expert,
 // out = bf16(out + bf16(shared * bf16(sigmoid(gate_logit)))) (:477-484).
+// With a residual (the decoder layer's FFN half), out = bf16(residual + out) last:
+// residual.add(ff.forward(h)), qwen3_moe_python_port.rs:736-739 and
+// lfm2_moe_python_port.rs:856-868.
 // Each thread owns 8 consecutive hidden elements of one token (16-byte loads/stores).
 //
 // rms_norm: y = bf16(bf16(x * r) * w), r = 1 / sqrt(sum(x^2) / dim + eps) with IEEE
@@ -65,6 +68,15 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
       float s = (i & 1) ? bf_hi(u[i >> 1]) : bf_lo(u[i >> 1]);
       if (gated) s = rbf(__fmul_rn(s, gv));
       o[i] = f2bf(__fadd_rn(bf2f(o[i]), s));
+    }
+  }
+  if (a.residual) {
+    const uint4 v = *reinterpret_cast<const uint4*>(a.residual + (size_t)t * a.H + h);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float r = (i & 1) ? bf_hi(u[i >> 1]) : bf_lo(u[i >> 1]);
+      o[i] = f2bf(__fadd_rn(r, bf2f(o[i])));
     }
   }
   uint4 ov;

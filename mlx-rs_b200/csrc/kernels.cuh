@@ -113,6 +113,7 @@ struct CombineArgs {
   const uint16_t* weights;  // [T, k] bf16
   const uint16_t* shared;   // [T, H] shared expert output or null
   const uint16_t* gate_val; // [T] bf16 shared gate or null
+  const uint16_t* residual; // [T, H] added last (the decoder layer's residual) or null
   int T, k, H;
   uint16_t* out;            // [T, H]
 };

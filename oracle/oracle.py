@@ -244,6 +244,26 @@ def stack_forward(blocks, norm_weights, x, eps=1e-6, nthreads=0):
     return h
 
 
+def layer_ffn_forward(block, x, norm_weight, eps=1e-6, nthreads=0):
+    """The MoE half of a decoder layer: x + block(rms_norm(x)), the add in fp32 of the two
+    bf16 values rounded to bf16 (residual.add(ff.forward(post_attention_layernorm(x))),
+    qwen3_moe_python_port.rs:736-739; lfm2_moe_python_port.rs:856-868).
+    Returns (out, normed, idx, weights)."""
+    h = rms_norm(x, norm_weight, eps, nthreads)
+    y, idx, w = block_forward(block, h, nthreads)
+    xs = np.asarray(x, np.uint16).reshape(np.shape(y))
+    out = (_rbf(_f(xs) + _f(np.asarray(y, np.uint16))).view(np.uint32) >> 16).astype(np.uint16)
+    return out, h, idx, w
+
+
+def residual_stack_forward(blocks, norm_weights, x, eps=1e-6, nthreads=0):
+    """Decoder layers' FFN halves in sequence: h = h + block_l(rms_norm(h, w_l))."""
+    h = x
+    for blk, w in zip(blocks, norm_weights):
+        h, _, _, _ = layer_ffn_forward(blk, h, w, eps, nthreads)
+    return h
+
+
 # ----------------------------------------------------------------------------------
 # Expert parallelism: the block split over ranks by expert range (the reference runs on
 # one device; this restates its combine, qwen3_moe_python_port.rs:471-472, with the

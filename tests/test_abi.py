@@ -40,6 +40,7 @@ def test_null_context_is_rejected_without_crashing():
     lib = mlx_rs_b200.library()
     assert lib.moe_quantized_matmul(None, None, 1, 64, None, None, None, 1, 1, 64, 4, None) == _lib.MOE_ERR_INVALID
     assert lib.moe_block_forward(None, None, None, None, 1, None) == _lib.MOE_ERR_INVALID
+    assert lib.moe_layer_ffn_forward(None, None, None, None, 1, None, 1e-6, None, None) == _lib.MOE_ERR_INVALID
     assert lib.moe_ctx_create(0, None, None) == _lib.MOE_ERR_INVALID
     assert lib.moe_last_error(None) == b"null context"
 

@@ -338,3 +338,57 @@ def test_whole_k_scale_gemv_bit_identical(cfg_name, seed, T, monkeypatch):
         assert np.array_equal(u, v)
     y, _, _ = O.block_forward(bw, x)
     assert_close(got[0].reshape(T, -1), y, f"{cfg_name} whole-K scales vs oracle", ULP_TOL)
+
+
+# ----------------------------------------------------------------------------------
+# the decoder layer's FFN half: x + block(RmsNorm(x)), residual fused into the combine
+# ----------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("cfg_name,seed,T", [("QWEN3_30B_A3B", 1, 64), ("QWEN15_MOE_A27B", 2, 24),
+                                              ("LFM2_8B_A1B", 3, 512)])
+def test_layer_ffn_matches_oracle_and_unfused(cfg_name, seed, T):
+    """Normed rows bit-exact with the oracle's RMSNorm, routing bit-exact on them, the
+    fused residual bit-identical to block output + x added in bf16, and within tolerance
+    of the oracle layer."""
+    torch = _torch()
+    import oracle as O
+    from gpu_util import dev_bits, to_dev
+    cfg = getattr(S, cfg_name)
+    bw, blk = _block(cfg, seed)
+    x_bits = S.host_x(800 + T, T, cfg.hidden)
+    nw_bits = S.f32_to_bf16_bits(np.random.default_rng(seed).uniform(0.5, 1.5, cfg.hidden).astype(np.float32))
+    x, nw = to_dev(x_bits), to_dev(nw_bits)
+    normed = torch.empty_like(x)
+    out = blk.forward_layer(x, nw, 1e-6, normed=normed)
+    unfused = blk.forward(normed) + x
+    idx, w, _, _ = blk.route(normed)
+    torch.cuda.synchronize()
+    y, h_ref, idx_ref, w_ref = O.layer_ffn_forward(bw, x_bits, nw_bits, 1e-6)
+    assert np.array_equal(dev_bits(normed), h_ref), "RMSNorm differs"
+    assert np.array_equal(dev_bits(idx).reshape(idx_ref.shape), idx_ref), "routing differs"
+    assert np.array_equal(dev_bits(w).reshape(w_ref.shape), w_ref), "combine weights differ"
+    assert np.array_equal(dev_bits(out), dev_bits(unfused)), "fused residual differs from block + x"
+    tol = ULP_TOL_TC if T >= 512 else ULP_TOL
+    assert_close(dev_bits(out).reshape(y.shape), y, f"{cfg_name} layer vs oracle", tol)
+
+
+def test_residual_stack_and_layer_errors():
+    torch = _torch()
+    import oracle as O
+    from mlx_rs_b200._lib import MlxError
+    from mlx_rs_b200.block import MoeStack, RmsNorm
+    from gpu_util import dev_bits, make_block, to_dev
+    cfg = S.QWEN3_30B_A3B
+    bws = [S.host_block(cfg, 110 + l) for l in range(3)]
+    rng = np.random.default_rng(11)
+    norms = [S.f32_to_bf16_bits(rng.uniform(0.5, 1.5, cfg.hidden).astype(np.float32)) for _ in range(3)]
+    x = S.host_x(12, 32, cfg.hidden)
+    blocks = [make_block(b) for b in bws]
+    stack = MoeStack(blocks, [RmsNorm(to_dev(n), 1e-6) for n in norms], residual=True)
+    got = dev_bits(stack(to_dev(x)))
+    ref = O.residual_stack_forward(bws, norms, x, 1e-6)
+    assert_close(got.reshape(ref.shape), ref, "residual stack vs oracle", ULP_TOL)
+    xd = to_dev(x)
+    with pytest.raises(MlxError):
+        blocks[0].forward_layer(xd, to_dev(norms[0]), 1e-6, out=xd)  # out aliases x
+    torch.cuda.synchronize()

@@ -166,3 +166,18 @@ def test_golden_fixtures_reproduce():
     for fn in files:
         z = np.load(os.path.join(GOLDEN, fn))
         golden_cases.check_oracle_against_fixture(fn[:-4], z)
+
+
+def test_layer_ffn_oracle_is_norm_block_residual():
+    """x + block(rms_norm(x)): the add of two bf16 values in fp32, rounded to bf16."""
+    cfg = S.MoeConfig(256, 8, 2, 128, 0, S.SCORING_SOFTMAX, True, False)
+    bw = S.host_block(cfg, 5)
+    x = S.host_x(6, 5, 256)
+    nw = S.f32_to_bf16_bits(np.linspace(0.5, 1.5, 256, dtype=np.float32))
+    out, h, idx, w = O.layer_ffn_forward(bw, x, nw, 1e-6)
+    assert np.array_equal(h, O.rms_norm(x, nw, 1e-6))
+    y, idx2, w2 = O.block_forward(bw, h)
+    assert np.array_equal(idx, idx2) and np.array_equal(w, w2)
+    assert np.array_equal(out, S.f32_to_bf16_bits(S.bf16_bits_to_f32(x) + S.bf16_bits_to_f32(y)))
+    two = O.residual_stack_forward([bw, bw], [nw, nw], x, 1e-6)
+    assert np.array_equal(two, O.layer_ffn_forward(bw, out, nw, 1e-6)[0])
