@@ -8,6 +8,8 @@ Host-side mirror of the reference's Rust interface for this path:
       <- SparseMoeBlock::forward (qwen3_moe_python_port.rs:420-488),
          MoeFeedForward::forward (lfm2_moe_python_port.rs:541-740),
          RmsNorm::forward (crates/mlx-nn/src/rms_norm.rs:30-34)
+  graph.GraphedForward
+      <- the per-step MoE work of the decode loop (generate.rs:811-880), one graph replay
   checkpoint.load_blocks / load_device_blocks
       <- VarBuilder::from_safetensors + SparseMoeBlock::load / MoeFeedForward::load
          (crates/mlx-nn/src/var_builder.rs:31-46, qwen3_moe_python_port.rs:394-418,
@@ -20,5 +22,6 @@ from . import ops  # noqa: F401
 from . import block  # noqa: F401
 from . import synth  # noqa: F401
 from . import checkpoint  # noqa: F401
+from . import graph  # noqa: F401
 
-__all__ = ["MlxError", "library", "library_path", "ops", "block", "synth", "checkpoint"]
+__all__ = ["MlxError", "library", "library_path", "ops", "block", "synth", "checkpoint", "graph"]
