@@ -126,10 +126,11 @@ struct RowMap {
 //         8-byte fragment reads conflict-free; then [MT*16 rows][4] bf16 scales and
 //         [MT*16 rows][4] bf16 biases of the chunk's groups (copied with the weights, so
 //         no scale load is outstanding in registers across a chunk).
-// FK (whole-K scales, 16-warp CTAs): the stages hold weights only; each warp's scales
-// and biases for all of K sit in one region per warp, copied once per launch with
-// coalesced 16-byte cp.async (the unit's rows are contiguous in the MLX layout), so
-// every 32-byte sector of the scale arrays is fetched once instead of once per chunk:
+// FK (whole-K scales; 16-warp CTAs for long K, 8-warp below): the stages hold weights
+// only; each warp's scales and biases for all of K sit in one region per warp, copied
+// once per CTA with coalesced 16-byte cp.async (the unit's rows are contiguous in the
+// MLX layout), so every 32-byte sector of the scale arrays is fetched once instead of
+// once per chunk:
 //   sregion [warps][s: ring rows][G] bf16, [b: ring rows][G] bf16 (gated: the MT*8 gate
 //           rows, then the MT*8 up rows), between xsum and the rings.
 template <bool GATED, int MT, int NC, int NS, bool SPLIT, bool FK = false>
@@ -218,10 +219,10 @@ __global__ void __launch_bounds__(FK ? 512 : 256) qgemv_kernel(QgemvArgs a, int 
     for (int i = 0; i < kPieces; ++i) src[i] += (size_t)c_begin * kKC * 8;
   }
   int issued = 0;  // chunks issued so far in this token chunk
-  // Scales and biases travel with the weights into the stage: 8-byte cp.async when G % 4
-  // == 0 and the bases are 8-byte aligned, two 4-byte ones when G is even and they are
-  // 4-byte aligned, otherwise plain loads and shared stores at issue time (odd G, or no
-  // biases: zeros).
+  // Without FK, scales and biases travel with the weights into the stage: 8-byte
+  // cp.async when G % 4 == 0 and the bases are 8-byte aligned, two 4-byte ones when G is
+  // even and they are 4-byte aligned, otherwise plain loads and shared stores at issue
+  // time (odd G, or no biases: zeros).
   const uintptr_t align_bits = reinterpret_cast<uintptr_t>(a.s0) | reinterpret_cast<uintptr_t>(a.b0) |
                                (GATED ? (reinterpret_cast<uintptr_t>(a.s1) | reinterpret_cast<uintptr_t>(a.b1)) : 0);
   const bool has_b = a.b0 != nullptr && (!GATED || a.b1 != nullptr);
