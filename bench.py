@@ -306,20 +306,23 @@ def events():
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
 
-def e2e_run(args, fwd, xs_host_bits, out_shape, dev, timer):
-    """Mean ms of H2D (pinned) + forward + D2H per step, max over ranks."""
+def e2e_run(args, fwd, xs_host_bits, out_shape, dev, timer, graphed=None):
+    """Mean ms of H2D (pinned) + forward + D2H per step, max over ranks. With `graphed`
+    (a graph.GraphedForward), each step copies the host tokens straight into its input
+    buffer and replays it: the public decode-step API."""
     import numpy as np
     import torch
     stream = torch.cuda.current_stream(dev)
     xs_pin = [torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).pin_memory() for x in xs_host_bits]
     out_pin = torch.empty(*out_shape, dtype=torch.bfloat16).pin_memory()
-    xdev = torch.empty(xs_pin[0].shape, dtype=torch.bfloat16, device=dev)
+    xdev = graphed.static_x if graphed is not None else torch.empty(xs_pin[0].shape, dtype=torch.bfloat16,
+                                                                     device=dev)
     times = []
     for i in range(args.warmup + args.steps):
         a, b = events()
         a.record(stream)
         xdev.copy_(xs_pin[i % len(xs_pin)], non_blocking=True)
-        y = fwd(xdev)
+        y = graphed.replay() if graphed is not None else fwd(xdev)
         out_pin.copy_(y, non_blocking=True)
         b.record(stream)
         b.synchronize()
@@ -518,7 +521,21 @@ def run_block(args, dev):
         roof["traffic"] = NCU_TRAFFIC[(args.workload, dom)]
         roof["traffic_source"] = "ncu --set full capture of this workload (one launch)"
 
-    e2e = e2e_run(args, lambda xd: blk.forward(xd, out), xs_host, (T, H), dev, timer)
+    # end to end through the public API: the block captured once (graph.GraphedForward)
+    # and replayed per step, host tokens in and the step's output back every step
+    e2e_api = "graph.GraphedForward(SparseMoeBlock.forward), pinned H2D + replay + D2H per step"
+    graphed = None
+    if not args.no_graph:
+        try:
+            from mlx_rs_b200.graph import GraphedForward
+            out_g = torch.empty_like(out)
+            graphed = GraphedForward(lambda xd: blk.forward(xd, out_g), xs[0])
+        except Exception as ex:  # eager public API instead
+            graphed = None
+            e2e_api = f"SparseMoeBlock.forward eager (graph capture failed: {type(ex).__name__})"
+    if graphed is None and args.no_graph:
+        e2e_api = "SparseMoeBlock.forward eager, pinned H2D + forward + D2H per step"
+    e2e = e2e_run(args, lambda xd: blk.forward(xd, out), xs_host, (T, H), dev, timer, graphed)
 
     sweep = {}
     if not args.no_sweep and regime == "decode" and args.workload == "decode":
@@ -560,7 +577,7 @@ def run_block(args, dev):
         "roofline": roof,
         "cpu_baseline": cpu,
         "e2e": {"value": T / (e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
-                "d2h_bytes_per_step": T * H * 2, "ms_per_step": e2e},
+                "d2h_bytes_per_step": T * H * 2, "ms_per_step": e2e, "api": e2e_api},
         "gpu_launches": launches * args.steps,
         "clocks": clock_info,
         "library": mlx_rs_b200.library_path,
