@@ -505,30 +505,30 @@ __global__ void __launch_bounds__(FK ? 512 : 256) qgemv_kernel(QgemvArgs a, int 
             }
           }
         }
-      continue;
-    }
+    } else {
 #pragma unroll
-    for (int n = 0; n < NC; ++n)
+      for (int n = 0; n < NC; ++n)
 #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        const int tok = n * kTok + 2 * cq + cc;
-        if (tok < ntok) {
-          const int64_t pos = cbase + tok;
-          const int64_t orow = a.out_mode == 0 ? pos : rm.orig(pos);
-          uint16_t* o = a.out + (size_t)orow * N;
+        for (int cc = 0; cc < 2; ++cc) {
+          const int tok = n * kTok + 2 * cq + cc;
+          if (tok < ntok) {
+            const int64_t pos = cbase + tok;
+            const int64_t orow = a.out_mode == 0 ? pos : rm.orig(pos);
+            uint16_t* o = a.out + (size_t)orow * N;
 #pragma unroll
-          for (int t = 0; t < MT; ++t) {
-            if (GATED) {
-              const int row = r0 + 8 * t + gq;
-              if (row < N) o[row] = swiglu_bf16(rbf(acc[n][t][cc]), rbf(acc[n][t][2 + cc]));
-            } else {
-              const int row = r0 + 16 * t + gq;
-              if (row < N) o[row] = f2bf(acc[n][t][cc]);
-              if (row + 8 < N) o[row + 8] = f2bf(acc[n][t][2 + cc]);
+            for (int t = 0; t < MT; ++t) {
+              if (GATED) {
+                const int row = r0 + 8 * t + gq;
+                if (row < N) o[row] = swiglu_bf16(rbf(acc[n][t][cc]), rbf(acc[n][t][2 + cc]));
+              } else {
+                const int row = r0 + 16 * t + gq;
+                if (row < N) o[row] = f2bf(acc[n][t][cc]);
+                if (row + 8 < N) o[row + 8] = f2bf(acc[n][t][2 + cc]);
+              }
             }
           }
         }
-      }
+    }
   }
 }
 
