@@ -424,3 +424,15 @@ def test_graphed_residual_stack_bit_identical_to_eager():
         got = dev_bits(g(x))
         assert np.array_equal(got, want)
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("cfg,T", [
+    (S.MoeConfig(256, 512, 32, 128, 0, S.SCORING_SOFTMAX, True, False, name="max-experts-topk"), 17),
+    (S.MoeConfig(256, 512, 32, 128, 0, S.SCORING_SOFTMAX, False, False, name="max-experts-topk"), 1),
+    (S.MoeConfig(256, 1, 1, 128, 0, S.SCORING_SOFTMAX, False, False, name="one-expert"), 9),
+    (S.MoeConfig(256, 3, 2, 128, 0, S.SCORING_SIGMOID_BIAS_SELECT, True, False, name="three-experts"), 13),
+])
+def test_extreme_shapes_match_oracle(cfg, T):
+    """The ABI's limits (512 experts, top-32) and the smallest expert sets: routing and
+    grouping bit-exact, outputs within tolerance."""
+    _live(cfg, 31, T)

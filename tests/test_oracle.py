@@ -148,6 +148,9 @@ def test_rms_norm_against_float64():
     ("qwen3_renorm", S.MoeConfig(256, 16, 8, 64, 0, S.SCORING_SOFTMAX, True, False), 5),
     ("lfm2_sigmoid", S.MoeConfig(128, 8, 2, 128, 0, S.SCORING_SIGMOID_BIAS_SELECT, True, False), 7),
     ("lfm2_softmax_bias", S.MoeConfig(128, 8, 2, 64, 0, S.SCORING_SOFTMAX_BIAS, False, False), 4),
+    ("max_experts_topk", S.MoeConfig(128, 512, 32, 64, 0, S.SCORING_SOFTMAX, True, False), 3),
+    ("one_expert", S.MoeConfig(128, 1, 1, 64, 0, S.SCORING_SOFTMAX, False, False), 3),
+    ("three_experts_sigmoid", S.MoeConfig(128, 3, 2, 64, 0, S.SCORING_SIGMOID_BIAS_SELECT, True, False), 4),
 ])
 def test_block_oracle_vs_numpy_restatement(name, cfg, T):
     bw = S.host_block(cfg, 21)
