@@ -101,6 +101,25 @@ MOE_DEV void cp_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
+// u8 x s8 -> s32 MMA, k = 32 per instruction.
+MOE_DEV void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1,
+                  bool first) {
+  if (first) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+MOE_DEV float i2f(int v) { return (float)v; }
+
 // Piece swizzle of the whole-K scale regions (16-byte pieces within a row).
 MOE_DEV int fk_swz(int r, int G) { return (G & 31) == 0 ? ((r >> 1) & 3) : 0; }
 
@@ -532,6 +551,279 @@ __global__ void __launch_bounds__(FK ? 512 : 256) qgemv_kernel(QgemvArgs a, int 
   }
 }
 
+// Integer path (decode, whole-K scales, MT = 2, 4 tokens per pass): weights enter the MMA
+// as u8 nibbles (w & 0x0f0f0f0f even nibbles, (w >> 4) & 0x0f0f0f0f odd nibbles), tokens as
+// two s8 limbs of a per-token fixed-point mantissa m = rint(x * 2^-E), |m| < 2^14,
+// m = 128 * hi + lo, lo in [0, 127]. MMA columns n = 2t + limb (t = token 0..3), so a
+// lane's C fragment holds one token's (hi, lo) sums for rows gq and gq+8:
+//   sum_k x*(s*q + b) = 2^E * (s * (128*D_hi + D_lo) + b * X'),  X' = sum_k m.
+// k-permutation per 32-k MMA (word 2cq for MMA 0, 2cq+1 for MMA 1 of a group): k-slots
+// 4cq+i hold element 16cq + 2i (+8 for MMA 1), k-slots 16+4cq+i element 16cq + 2i + 1.
+// Shared memory: xq [8 columns][K + 64 B] s8 limbs in fragment order, xs [G][4] float X',
+// emax [4] int, scale regions (as FK), rings (weights only).
+template <bool GATED>
+__global__ void __launch_bounds__(512) qgemv_i8_kernel(QgemvArgs a, int units_per_expert, int ctas_per_expert,
+                                                       int max_slots) {
+  constexpr int MT = 2, NS = 2;
+  constexpr int ROWS = GATED ? 8 * MT : 16 * MT;
+  constexpr int TOK = 4;
+  constexpr int kCols = 8;
+  constexpr int kRingRows = MT * 16;
+  constexpr int kStageBytes = kRingRows * kKC * 32;
+  constexpr int kPieces = kRingRows * kKC * 2 / 32;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int gq = lane >> 2, cq = lane & 3;
+  const int slot = blockIdx.x / ctas_per_expert;
+  const int ut = (blockIdx.x - slot * ctas_per_expert) * nwarps + warp;
+  pdl_wait();
+  if (slot >= max_slots) return;
+  if (a.n_active && slot >= *a.n_active) return;
+  const int e = a.active ? a.active[slot] : slot;
+  const int64_t row_begin = a.offsets ? a.offsets[e] : 0;
+  const int64_t row_end = a.offsets ? a.offsets[e + 1] : a.n_identity;
+  if (row_end <= row_begin) return;
+  if (a.max_expert_rows && row_end - row_begin >= a.max_expert_rows) return;
+  const int K = a.K, N = a.N, G = K >> 6, wpr = K >> 3;
+  const int r0 = ut * ROWS;
+  const bool unit_live = ut < units_per_expert && r0 < N;
+  const RowMap rm{a.x_mode, a.x_repeat, a.lhs, a.perm};
+
+  const int col_bytes = K + 64;  // 16-word column offset: conflict-free 16-byte fragment reads
+  const uint32_t smem_s = (uint32_t)__cvta_generic_to_shared(smem);
+  const uint32_t xq_s = smem_s;
+  const uint32_t xs_s = xq_s + kCols * col_bytes;
+  float* xs = reinterpret_cast<float*>(smem + kCols * col_bytes);           // [G][TOK]
+  int* emax = reinterpret_cast<int*>(smem + kCols * col_bytes + G * TOK * 4);  // [TOK]
+  const uint32_t sreg_all = xs_s + G * TOK * 4 + 16;
+  const uint32_t sreg_s = sreg_all + (uint32_t)(warp * kRingRows * G * 4);
+  const uint32_t ring_s = sreg_all + (uint32_t)(nwarps * kRingRows * G * 4) + (uint32_t)(warp * NS * kStageBytes);
+
+  auto wrow = [&](int rr) -> const uint32_t* {
+    const int t = rr >> 4, r = rr & 15;
+    int row;
+    const uint32_t* W;
+    if (GATED) {
+      row = r0 + 8 * t + (r & 7);
+      W = (r < 8) ? a.w0 : a.w1;
+    } else {
+      row = r0 + 16 * t + r;
+      W = a.w0;
+    }
+    row = row < N ? row : N - 1;
+    return W + ((size_t)e * N + row) * wpr;
+  };
+  const uint32_t* src[kPieces];
+  uint32_t dst[kPieces];
+#pragma unroll
+  for (int i = 0; i < kPieces; ++i) {
+    const int q = i * 32 + lane;
+    const int rr = q >> 3, part = q & 7, gl = part >> 1, half = part & 1;
+    src[i] = wrow(rr) + part * 4;
+    dst[i] = rr * (kKC * 32) + ((gl ^ (rr & 3)) * 32) + half * 16;
+  }
+  const int nchunks = G / kKC;  // the launcher requires G % 4 == 0
+  int issued = 0;
+  auto issue_chunk = [&](int c) {
+    const uint32_t st = ring_s + (uint32_t)((c % NS) * kStageBytes);
+#pragma unroll
+    for (int i = 0; i < kPieces; ++i) cp_async16(st + dst[i], src[i]);
+#pragma unroll
+    for (int i = 0; i < kPieces; ++i) src[i] += kKC * 8;
+    ++issued;
+    cp_commit();
+  };
+  auto reset_src = [&]() {
+#pragma unroll
+    for (int i = 0; i < kPieces; ++i) src[i] -= (size_t)issued * kKC * 8;
+    issued = 0;
+  };
+  if (unit_live) {  // whole-K scale regions, as in qgemv_kernel's FK mode
+    constexpr int kRegions = GATED ? 4 : 2;
+    const int rrows = GATED ? MT * 8 : MT * 16;
+    const int rbytes = rrows * G * 2;
+    const int npieces = G / 8;
+#pragma unroll
+    for (int rg = 0; rg < kRegions; ++rg) {
+      const uint16_t* base = GATED ? (rg == 0 ? a.s0 : rg == 1 ? a.s1 : rg == 2 ? a.b0 : a.b1)
+                                   : (rg == 0 ? a.s0 : a.b0);
+      const unsigned char* srcb = reinterpret_cast<const unsigned char*>(base + ((size_t)e * N + r0) * G);
+      const uint32_t dstb = sreg_s + (uint32_t)(rg * rbytes);
+      if ((G & 31) == 0) {
+        for (int idx = lane; idx < rrows * npieces; idx += 32) {
+          const int r = idx / npieces, pc = idx - r * npieces;
+          cp_async16(dstb + r * G * 2 + ((pc ^ fk_swz(r, G)) << 4), srcb + r * G * 2 + (pc << 4));
+        }
+      } else {
+        for (int off = lane * 16; off < rbytes; off += 32 * 16) cp_async16(dstb + off, srcb + off);
+      }
+    }
+  }
+
+  for (int64_t cbase = row_begin; cbase < row_end; cbase += TOK) {
+    const int ntok = (row_end - cbase < TOK) ? (int)(row_end - cbase) : TOK;
+    reset_src();
+    if (unit_live) issue_chunk(0);
+    __syncthreads();  // previous pass's readers of xq / xs / emax are done
+    // ---- stage: per-token largest magnitude, then the limbs in fragment order and X'
+    const int units = ntok * G * 4;
+    for (int i = tid; i < TOK; i += blockDim.x) emax[i] = 0;
+    __syncthreads();
+    for (int u = tid; u < units; u += blockDim.x) {
+      const int c = u & 3, g = (u >> 2) % G, t = (u >> 2) / G;
+      const uint4* p = reinterpret_cast<const uint4*>(a.x + (size_t)rm.xrow(cbase + t) * K + g * 64 + c * 16);
+      const uint4 v0 = p[0], v1 = p[1];
+      const uint32_t in[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      uint32_t m = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m = max(m, max(in[i] & 0x7fffu, (in[i] >> 16) & 0x7fffu));
+      atomicMax(&emax[t], (int)m);
+    }
+    __syncthreads();
+    for (int u0 = 0; u0 < units; u0 += blockDim.x) {  // uniform trip count (shuffles below)
+      const int u = u0 + tid;
+      const bool uvalid = u < units;
+      const int c = u & 3, g = (u >> 2) % G, t = (u >> 2) / G;
+      int mi[16];
+      if (uvalid) {
+        const uint4* p = reinterpret_cast<const uint4*>(a.x + (size_t)rm.xrow(cbase + t) * K + g * 64 + c * 16);
+        const uint4 v0 = p[0], v1 = p[1];
+        const uint32_t in[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        // 2^-E with the row's largest |x| * 2^-E in [2^13, 2^14) (zero / non-finite rows: E = 0)
+        const int mb = emax[t];
+        int sh = 0;
+        if (mb != 0 && mb < 0x7f80) {
+          const int ex = (mb >> 7) - 127;  // floor(log2 max) for normal values
+          sh = 13 - (ex < -126 ? -126 : ex);
+          sh = sh > 126 ? 126 : sh;
+        }
+        const float sc = __int_as_float((sh + 127) << 23);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          mi[2 * i] = __float2int_rn(bf_lo(in[i]) * sc);
+          mi[2 * i + 1] = __float2int_rn(bf_hi(in[i]) * sc);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) mi[i] = 0;
+      }
+      int xsum = 0;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) xsum += mi[i];
+      xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
+      xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
+      if (uvalid) {
+        // column 2t: hi limbs, 2t+1: lo limbs; 16 bytes per (column, group, quarter):
+        // [e0 e2 e4 e6 | e1 e3 e5 e7 | e8 e10 e12 e14 | e9 e11 e13 e15]
+        auto pack = [&](int i0, int limb) -> uint32_t {
+          uint32_t r = 0;
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const int m = mi[i0 + 2 * b];
+            const int v = limb ? (m & 127) : (m >> 7);
+            r |= ((uint32_t)v & 0xffu) << (8 * b);
+          }
+          return r;
+        };
+#pragma unroll
+        for (int limb = 0; limb < 2; ++limb) {
+          const uint4 o = make_uint4(pack(0, limb), pack(1, limb), pack(8, limb), pack(9, limb));
+          *reinterpret_cast<uint4*>(smem + (size_t)(2 * t + limb) * col_bytes + g * 64 + c * 16) = o;
+        }
+        if (c == 0) xs[g * TOK + t] = (float)xsum;
+      }
+    }
+    for (int i = tid; i < G * TOK; i += blockDim.x)
+      if ((i % TOK) >= ntok) xs[i] = 0.0f;
+    __syncthreads();
+    if (!unit_live) continue;
+
+    const uint32_t xb = xq_s + gq * col_bytes + cq * 16;  // column gq's fragment base
+    float acc[MT][2];  // [tile][row gq / gq+8], token cq
+#pragma unroll
+    for (int t = 0; t < MT; ++t) acc[t][0] = acc[t][1] = 0.0f;
+    for (int c = 0; c < nchunks; ++c) {
+      if (c + 1 < nchunks) issue_chunk(c + 1);
+      else cp_commit();
+      const int g0 = c * kKC;
+      cp_wait<NS - 1>();
+      __syncwarp();
+      const uint32_t st = ring_s + (uint32_t)((c % NS) * kStageBytes);
+      uint2 sw[MT][2], bw[MT][2];
+#pragma unroll
+      for (int t = 0; t < MT; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = GATED ? t * 8 + gq : t * 16 + gq + 8 * h;
+          const int fr = GATED ? h * (MT * 8) + r : r;
+          const uint32_t so = sreg_s + (uint32_t)(fr * G * 2 + ((((g0 >> 3) ^ fk_swz(r, G))) << 4) + (g0 & 7) * 2);
+          sw[t][h] = lds_u2(so);
+          bw[t][h] = lds_u2(so + kRingRows * G * 2);
+        }
+#pragma unroll
+      for (int gl = 0; gl < kKC; ++gl) {
+        const int g = g0 + gl;
+        const uint4 bf = lds_u4(xb + g * 64);           // (b0, b1) of MMA 0, (b0, b1) of MMA 1
+        const float X = xs[g * TOK + cq];
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+          const int rr = t * 16 + gq;
+          const uint32_t off = ((gl ^ (rr & 3)) * 32) + cq * 8;
+          const uint2 wlo = lds_u2(st + rr * (kKC * 32) + off);
+          const uint2 whi = lds_u2(st + (rr + 8) * (kKC * 32) + off);
+          int d[4];
+          imma(d, wlo.x & 0x0f0f0f0fu, whi.x & 0x0f0f0f0fu, (wlo.x >> 4) & 0x0f0f0f0fu, (whi.x >> 4) & 0x0f0f0f0fu,
+               bf.x, bf.y, true);
+          imma(d, wlo.y & 0x0f0f0f0fu, whi.y & 0x0f0f0f0fu, (wlo.y >> 4) & 0x0f0f0f0fu, (whi.y >> 4) & 0x0f0f0f0fu,
+               bf.z, bf.w, false);
+          const uint32_t s_lo2 = (gl >> 1) ? sw[t][0].y : sw[t][0].x;
+          const uint32_t s_hi2 = (gl >> 1) ? sw[t][1].y : sw[t][1].x;
+          const uint32_t b_lo2 = (gl >> 1) ? bw[t][0].y : bw[t][0].x;
+          const uint32_t b_hi2 = (gl >> 1) ? bw[t][1].y : bw[t][1].x;
+          const float s_l = (gl & 1) ? bf_hi(s_lo2) : bf_lo(s_lo2);
+          const float s_h = (gl & 1) ? bf_hi(s_hi2) : bf_lo(s_hi2);
+          const float b_l = (gl & 1) ? bf_hi(b_lo2) : bf_lo(b_lo2);
+          const float b_h = (gl & 1) ? bf_hi(b_hi2) : bf_lo(b_hi2);
+          // (hi, lo) sums of token cq: c0/c1 row gq, c2/c3 row gq+8 (exact below 2^24)
+          const float v_l = __fmaf_rn(128.0f, i2f(d[0]), i2f(d[1]));
+          const float v_h = __fmaf_rn(128.0f, i2f(d[2]), i2f(d[3]));
+          acc[t][0] = __fmaf_rn(b_l, X, __fmaf_rn(s_l, v_l, acc[t][0]));
+          acc[t][1] = __fmaf_rn(b_h, X, __fmaf_rn(s_h, v_h, acc[t][1]));
+        }
+      }
+      __syncwarp();
+    }
+    cp_wait<0>();
+    pdl_trigger();
+    // ---- epilogue: token cq, rows gq / gq+8 of each tile; undo 2^-E
+    const int tok = cq;
+    if (tok < ntok) {
+      const int mb = emax[tok];
+      int sh = 0;
+      if (mb != 0 && mb < 0x7f80) {
+        const int ex = (mb >> 7) - 127;
+        sh = 13 - (ex < -126 ? -126 : ex);
+        sh = sh > 126 ? 126 : sh;
+      }
+      const float us = __int_as_float((127 - sh) << 23);  // 2^-sh, sh in [-114, 126]
+      const int64_t pos = cbase + tok;
+      const int64_t orow = a.out_mode == 0 ? pos : rm.orig(pos);
+      uint16_t* o = a.out + (size_t)orow * N;
+#pragma unroll
+      for (int t = 0; t < MT; ++t) {
+        if (GATED) {
+          const int row = r0 + 8 * t + gq;
+          if (row < N) o[row] = swiglu_bf16(rbf(acc[t][0] * us), rbf(acc[t][1] * us));
+        } else {
+          const int row = r0 + 16 * t + gq;
+          if (row < N) o[row] = f2bf(acc[t][0] * us);
+          if (row + 8 < N) o[row + 8] = f2bf(acc[t][1] * us);
+        }
+      }
+    }
+  }
+}
+
 // Split-K reduction: out[row(pos), n] from the ksplit fp32 partials, added in split
 // order, then SwiGLU (gated, the exact bf16 sequence of the GEMV epilogue) or bf16
 // rounding. Rows of experts that the GEMV skipped (max_expert_rows) are left alone.
@@ -662,8 +954,37 @@ static int fk_warps(const QgemvArgs& a, bool gated) {
   return 0;
 }
 
+template <bool GATED>
+static cudaError_t launch_i8(const QgemvArgs& a, int slots, int wpc, cudaStream_t st) {
+  constexpr int ROWS = GATED ? 16 : 32;
+  const int upe = (a.N + ROWS - 1) / ROWS;
+  const int cpe = (upe + wpc - 1) / wpc;
+  const long long blocks = (long long)cpe * slots;
+  const int G = a.K / 64;
+  const size_t smem = (size_t)8 * (a.K + 64) + (size_t)G * 4 * 4 + 16 + (size_t)wpc * 32 * G * 4 +
+                      (size_t)wpc * 2 * 32 * kKC * 32;
+  if (smem > 227 * 1024 || blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  static thread_local int set_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != set_dev) {
+    cudaError_t err = cudaFuncSetAttribute(qgemv_i8_kernel<GATED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           227 * 1024);
+    if (err != cudaSuccess) return err;
+    set_dev = dev;
+  }
+  return launch_k(qgemv_i8_kernel<GATED>, dim3((unsigned)blocks), dim3(wpc * 32), smem, st, a, upe, cpe, slots);
+}
+
 template <bool GATED, int NC>
 static cudaError_t launch_qgemv_nc(const QgemvArgs& a, int slots, bool wide, cudaStream_t st) {
+  {
+    const char* env = std::getenv("MOE_B200_GEMV_I8");  // prototype: integer MMA path
+    if (env && env[0] == '1' && NC == 1 && wide && (a.K / 64) % 4 == 0) {
+      const int fw = fk_warps(a, GATED);
+      if (fw) return launch_i8<GATED>(a, slots, fw, st);
+    }
+  }
   if (NC == 1 && wide) {
     const int fw = fk_warps(a, GATED);
     if (fw) return launch_qgemv_t<GATED, 2, 1, 2, true>(a, slots, fw, st);

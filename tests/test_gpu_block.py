@@ -436,3 +436,20 @@ def test_extreme_shapes_match_oracle(cfg, T):
     """The ABI's limits (512 experts, top-32) and the smallest expert sets: routing and
     grouping bit-exact, outputs within tolerance."""
     _live(cfg, 31, T)
+
+
+@pytest.mark.parametrize("cfg_name,seed,T", [("QWEN3_30B_A3B", 1, 64), ("LFM2_8B_A1B", 3, 32)])
+def test_int8_gemv_path_matches_oracle(cfg_name, seed, T, monkeypatch):
+    """The opt-in integer decode GEMV (u8 weights, two s8 limbs of each token row, int32
+    MMA): routing unchanged, outputs within the parity tolerance of the oracle."""
+    import oracle as O
+    from gpu_util import run_block
+    cfg = getattr(S, cfg_name)
+    bw, blk = _block(cfg, seed)
+    x = S.host_x(900 + T, T, cfg.hidden)
+    monkeypatch.setenv("MOE_B200_GEMV_I8", "1")
+    got = run_block(blk, x)
+    y, idx, w = O.block_forward(bw, x)
+    assert np.array_equal(got[1].reshape(idx.shape), idx)
+    assert np.array_equal(got[2].reshape(w.shape), w)
+    assert_close(got[0].reshape(T, -1), y, f"{cfg_name} int8 GEMV vs oracle", ULP_TOL)
