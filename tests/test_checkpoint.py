@@ -215,3 +215,44 @@ def test_checkpoint_block_on_gpu_matches_oracle(tmp_path):
     assert np.array_equal(idx.reshape(ridx.shape), ridx), "expert indices differ"
     assert np.array_equal(w.reshape(rw.shape), rw), "combine weights differ"
     assert_close(out.reshape(y.shape), y, "checkpoint block vs oracle", ULP_TOL)
+
+
+def test_qwen_prestacked_switch_mlp_and_f16_scales(tmp_path):
+    """mlx-lm style Qwen checkpoints hold the experts pre-stacked under mlp.switch_mlp; F16
+    scales/biases are rounded to bf16 (the device path's type); a config without a
+    quantization block takes the reference's defaults (group 64, 4 bits)."""
+    cfg = S.MoeConfig(256, 8, 2, 128, 0, S.SCORING_SOFTMAX, True, False, name="qwen3_moe")
+    bw = S.host_block(cfg, 80)
+    t = {}
+    p = "model.layers.0.mlp"
+    _q(p + ".gate", bw.router, t)
+    f16 = {}
+    for name in ("gate", "up", "down"):
+        q = getattr(bw, name)
+        t[f"{p}.switch_mlp.{name}_proj.weight"] = q.w
+        t[f"{p}.switch_mlp.{name}_proj.scales"] = S.bf16_bits_to_f32(q.scales).astype(np.float16)
+        t[f"{p}.switch_mlp.{name}_proj.biases"] = S.bf16_bits_to_f32(q.biases).astype(np.float16)
+    C.write_safetensors(str(tmp_path / "model.safetensors"), t, f16)
+    conf = {"model_type": "qwen3_moe", "hidden_size": 256, "moe_intermediate_size": 128, "num_experts": 8,
+            "num_experts_per_tok": 2, "norm_topk_prob": True, "num_hidden_layers": 1}
+    json.dump(conf, open(tmp_path / "config.json", "w"))
+    (got,) = C.load_blocks(str(tmp_path))
+    assert got.config.group_size == 64 and got.config.bits == 4
+    for name in ("gate", "up", "down"):
+        q, g = getattr(bw, name), getattr(got, name)
+        assert np.array_equal(q.w, g.w)
+        want = S.f32_to_bf16_bits(S.bf16_bits_to_f32(q.scales).astype(np.float16).astype(np.float32))
+        assert np.array_equal(g.scales, want)
+
+
+def test_mismatched_scale_shape_is_rejected(tmp_path):
+    """Scales with fewer groups than the packed width implies: the loader refuses the block."""
+    cfg = S.MoeConfig(256, 8, 2, 128, 0, S.SCORING_SOFTMAX, True, False)
+    bw = S.host_block(cfg, 81)
+    _write_lfm2(str(tmp_path), [S.with_scoring(bw, S.SCORING_SOFTMAX_BIAS, 1, 0.5)], [1], cfg, 2)
+    tensors, c = C.open_checkpoint(str(tmp_path))
+    e = tensors.t["model.layers.1.feed_forward.switch_mlp.up_proj.scales"]
+    tensors.t["model.layers.1.feed_forward.switch_mlp.up_proj.scales"] = C._Entry(e.dtype, (8, 128, 3),
+                                                                                np.asarray(e.array)[..., :3])
+    with pytest.raises(C.CheckpointError, match="up"):
+        C.load_block(tensors, "model.layers.1", c)
