@@ -115,7 +115,9 @@ int moe_abi_version(void);
  * Replaces Array::quantized_matmul (crates/mlx-core/src/ops.rs:592-637), i.e.
  * mlx_quantized_matmul(&out, x, w, scales, biases, transpose, gs, bits, "affine", s)
  * at ops.rs:622-633, as called by Linear::forward (crates/mlx-nn/src/linear.rs:117-128).
- * transpose must be nonzero (the only form the reference calls).
+ * transpose must be nonzero (the only form the reference calls). M >= 32 rows (with
+ * N % 128 == 0) run on the tcgen05 GEMM, fewer on the GEMV; the tcgen05 path rounds each
+ * dequantised weight to bf16 before the multiply (MLX's GPU qmm does the same).
  */
 int moe_quantized_matmul(moe_ctx* ctx, const void* x, int64_t M, int64_t K, const uint32_t* w,
                          const void* scales, const void* biases, int64_t N, int transpose,
@@ -132,6 +134,8 @@ int moe_quantized_matmul(moe_ctx* ctx, const void* x, int64_t M, int64_t K, cons
  * x_repeat = k; the down projection's x [T,k,1,I] is x_rows = T*k, x_repeat = 1.
  * w is [num_experts, N, K*bits/32]. sorted_indices is accepted and ignored (the
  * kernels always group rows by expert themselves). transpose must be nonzero.
+ * Each expert runs on the kernel its row count calls for, as in moe_block_forward:
+ * experts with 32 rows or more on the tcgen05 GEMM (N % 128 == 0), the rest on the GEMV.
  */
 int moe_gather_qmm(moe_ctx* ctx, const void* x, int64_t x_rows, int64_t K, int64_t x_repeat,
                    const uint32_t* lhs_indices, const uint32_t* w, const void* scales,
@@ -262,7 +266,9 @@ int moe_ep_finish(moe_ctx* ctx, const float* partials, int32_t world, int64_t ro
  * error message; its own scratch is not used. All calls on a device share the array:
  * calls that overlap on the GPU race, so order them. The first call on each device
  * looks up the array's device address (with that device current); make it before any
- * stream capture.
+ * stream capture. The arguments are checked as moe_gather_qmm checks them (same codes,
+ * same order) before the size limits. An expired bounded wait inside the tcgen05 GEMM
+ * is not reported through moe_ctx_status for this entry point (it has no status word).
  */
 #define MOE_NOALLOC_MAX_BATCH 4096
 #define MOE_NOALLOC_MAX_EXPERTS 512

@@ -20,23 +20,10 @@ import torch
 
 from . import ops
 from ._lib import BlockConfig, BlockWeights as _CWeights, MlxError, QWeight as _CQ, library
+from .checkpoint import infer_bits  # the shape rule of qwen3_moe_python_port.rs:221-239
 from .ops import _ctx, _ptr
 from .synth import (SCORING_SIGMOID_BIAS_SELECT, SCORING_SOFTMAX, SCORING_SOFTMAX_BIAS,
                     BlockWeights, MoeConfig, QWeight)
-
-
-def infer_bits(weight_shape, scales_shape, group_size: int, fallback: int) -> int:
-    """Bits per element from packed/scales shapes (qwen3_moe_python_port.rs:221-239)."""
-    packed = weight_shape[-1] if len(weight_shape) else 0
-    n_groups = scales_shape[-1] if len(scales_shape) else 0
-    if packed <= 0 or n_groups <= 0 or group_size <= 0:
-        return fallback
-    unpacked = n_groups * group_size
-    num = packed * 32
-    if num % unpacked != 0:
-        return fallback
-    b = num // unpacked
-    return b if b in (2, 4, 8) else fallback
 
 
 class SwitchLinear:

@@ -427,7 +427,8 @@ bool use_tc(int64_t rows, int64_t experts, int N, int K) {
   const char* v = std::getenv("MOE_B200_TC");
   if (v && v[0] == '0') return false;
   if (v && v[0] == '1') return true;
-  return rows >= 32 * experts;
+  // (grid.y of the tcgen05 launch holds the token tiles: at most 65535)
+  return rows >= 32 * experts && rows <= (int64_t)65535 * moe::kTcTileRows;
 }
 
 // Routed experts: each expert takes the path its own row count calls for, decided on
@@ -472,8 +473,65 @@ ExpertPlan plan_experts(int64_t P, int E, int I, int H) {
   }
   const int64_t big = p.min_rows ? std::min<int64_t>(E, P / p.min_rows) : std::min<int64_t>(E, P);
   p.max_tiles = (int)(P / moe::kTcTileRows + big + 1);
+  if (P / moe::kTcTileRows + big + 1 > 65535) {  // beyond grid.y: every expert on the GEMV
+    ExpertPlan g;
+    return g;
+  }
   return p;
 }
+
+}  // namespace
+
+// gather_qmm as one hybrid launch sequence (declared in kernels.cuh); shared by
+// moe_gather_qmm and moe_gather_qmm_noalloc, which differ only in where the scratch lives.
+cudaError_t moe::launch_gather_qmm(const moe::GatherCall& c, cudaStream_t st) {
+  // one matrix: the gate/up fields of the plan with I = N, H = K
+  const ExpertPlan plan = plan_experts(c.batch, c.E, c.N, c.K);
+  moe::GroupArgs ga = c.g;
+  ga.key = c.rhs;
+  ga.key_packed = 0;
+  ga.key_base = 0;
+  ga.P = c.batch;
+  ga.E = c.E;
+  ga.inv = nullptr;
+  ga.tile_rows = moe::kTcTileRows;
+  ga.tc_min_rows = plan.min_rows;
+  if (!plan.tc_gu) ga.tile_start = nullptr;
+  cudaError_t e = moe::launch_group(ga, st);
+  if (e != cudaSuccess) return e;
+  moe::QgemvArgs q{};
+  q.x = c.x;
+  q.x_mode = c.x_mode;
+  q.x_repeat = c.x_repeat;
+  q.lhs = c.lhs;
+  q.perm = ga.perm;
+  q.offsets = ga.offsets;
+  q.active = ga.active;
+  q.n_active = ga.n_active;
+  q.w0 = c.w;
+  q.s0 = c.s;
+  q.b0 = c.b;
+  q.N = c.N;
+  q.K = c.K;
+  q.out = c.out;
+  q.out_mode = 1;
+  q.num_experts_total = c.E;
+  const int slots = (int)std::min<int64_t>(c.batch, c.E);
+  const int rows_pe = (int)std::min<int64_t>((c.batch + slots - 1) / slots, 1 << 20);
+  if (plan.gemv_gu) {
+    q.max_expert_rows = plan.gemv_skip_gu;
+    e = moe::launch_qgemv(q, false, slots, rows_pe, st);
+    if (e != cudaSuccess) return e;
+  }
+  if (plan.tc_gu) {
+    q.max_expert_rows = 0;
+    moe::TcGemmArgs ta{q, ga.tile_start, c.E, plan.max_tiles, c.status};
+    e = moe::launch_tc_gemm(ta, false, st);
+  }
+  return e;
+}
+
+namespace {
 
 moe::QgemvArgs qgemv_args(const moe_qweight& m0, const moe_qweight* m1, int N, int K) {
   moe::QgemvArgs q{};
@@ -634,6 +692,27 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
 
 }  // namespace
 
+// Argument checks shared by moe_gather_qmm and moe_gather_qmm_noalloc (same codes and
+// order: quantization, transpose, shapes, pointers); MOE_OK for a valid call, including
+// batch == 0, which computes nothing.
+namespace moe_internal {
+int check_gather(moe_ctx* ctx, const char* fn, const void* x, int64_t K, int64_t x_repeat,
+                 const uint32_t* lhs_indices, const uint32_t* w, const void* scales, int64_t num_experts,
+                 int64_t N, const uint32_t* rhs_indices, int64_t batch, int transpose, int group_size, int bits,
+                 const void* out) {
+  int rc = check_quant(ctx, fn, K, group_size, bits);
+  if (rc) return rc;
+  if (!transpose) return fail(ctx, MOE_ERR_UNSUPPORTED, "%s: transpose=false is not implemented", fn);
+  if (batch < 0 || N <= 0 || N > INT32_MAX || num_experts <= 0 || num_experts > 4096 || batch > INT32_MAX)
+    return fail(ctx, MOE_ERR_INVALID, "%s: bad batch/N/num_experts", fn);
+  if (!lhs_indices && x_repeat <= 0) return fail(ctx, MOE_ERR_INVALID, "%s: x_repeat must be positive", fn);
+  if (batch == 0) return MOE_OK;
+  if (!x || !w || !scales || !rhs_indices || !out) return fail(ctx, MOE_ERR_INVALID, "%s: null pointer", fn);
+  if (!aligned16(x) || !aligned16(w)) return fail(ctx, MOE_ERR_INVALID, "%s: x and w must be 16-byte aligned", fn);
+  return MOE_OK;
+}
+}  // namespace moe_internal
+
 extern "C" {
 
 int moe_abi_version(void) { return MOE_B200_ABI_VERSION; }
@@ -698,6 +777,16 @@ int moe_quantized_matmul(moe_ctx* ctx, const void* x, int64_t M, int64_t K, cons
   q.x_mode = 0;
   q.n_identity = (int)M;
   q.out = static_cast<uint16_t*>(out);
+  if (use_tc(M, 1, (int)N, (int)K)) {
+    // many rows: the tcgen05 GEMM, as the block's shared expert (one "expert", token
+    // tiles in order); the context's status word records an expired bounded wait
+    rc = ensure_scratch(ctx, 256);
+    if (rc) return rc;
+    moe::TcGemmArgs ta{q, nullptr, 1, (int)((M + moe::kTcTileRows - 1) / moe::kTcTileRows),
+                       static_cast<int32_t*>(ctx->scratch)};
+    MOE_CUDA(ctx, moe::launch_tc_gemm(ta, false, ctx->stream));
+    return MOE_OK;
+  }
   MOE_CUDA(ctx, moe::launch_qgemv(q, false, 1, (int)std::min<int64_t>(M, 1 << 20), ctx->stream));
   return MOE_OK;
 }
@@ -710,61 +799,47 @@ int moe_gather_qmm(moe_ctx* ctx, const void* x, int64_t x_rows, int64_t K, int64
   (void)x_rows;
   if (!ctx) return MOE_ERR_INVALID;
   ctx->last_error.clear();
-  const char* fn = "moe_gather_qmm";
-  int rc = check_quant(ctx, fn, K, group_size, bits);
-  if (rc) return rc;
-  if (!transpose) return fail(ctx, MOE_ERR_UNSUPPORTED, "%s: transpose=false is not implemented", fn);
-  if (batch < 0 || N <= 0 || N > INT32_MAX || num_experts <= 0 || num_experts > 4096 || batch > INT32_MAX)
-    return fail(ctx, MOE_ERR_INVALID, "%s: bad batch/N/num_experts", fn);
-  if (!lhs_indices && x_repeat <= 0) return fail(ctx, MOE_ERR_INVALID, "%s: x_repeat must be positive", fn);
-  if (batch == 0) return MOE_OK;
-  if (!x || !w || !scales || !rhs_indices || !out) return fail(ctx, MOE_ERR_INVALID, "%s: null pointer", fn);
-  if (!aligned16(x) || !aligned16(w)) return fail(ctx, MOE_ERR_INVALID, "%s: x and w must be 16-byte aligned", fn);
+  int rc = moe_internal::check_gather(ctx, "moe_gather_qmm", x, K, x_repeat, lhs_indices, w, scales, num_experts, N,
+                                      rhs_indices, batch, transpose, group_size, bits, out);
+  if (rc || batch == 0) return rc;
   DeviceGuard g(ctx->device);
   if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
 
   const int E = (int)num_experts;
   const int seg = moe::group_seg(batch, E);
   const int64_t nseg = std::max<int64_t>(1, (batch + seg - 1) / seg);
-  Carve size_only(nullptr);
-  size_only.take<int32_t>(nseg * E);
-  size_only.take<int32_t>(nseg * E);
-  size_only.take<int32_t>(E + 1);
-  size_only.take<int32_t>(E);
-  size_only.take<int32_t>(1);
-  size_only.take<uint32_t>(batch);
-  rc = ensure_scratch(ctx, size_only.off + 256);
+  auto carve = [&](void* base, moe::GroupArgs& ga, int32_t*& status) {
+    Carve cv(base);
+    status = cv.take<int32_t>(64);  // the context's status word, at offset 0
+    ga.hist = cv.take<int32_t>(nseg * E);
+    ga.segbase = cv.take<int32_t>(nseg * E);
+    ga.offsets = cv.take<int32_t>(E + 1);
+    ga.active = cv.take<int32_t>(E);
+    ga.n_active = cv.take<int32_t>(1);
+    ga.tile_start = cv.take<int32_t>(E + 1);
+    ga.perm = cv.take<uint32_t>(batch);
+    return cv.off + 256;
+  };
+  moe::GatherCall gc{};
+  rc = ensure_scratch(ctx, carve(nullptr, gc.g, gc.status));
   if (rc) return rc;
-  Carve cv(ctx->scratch);
-  moe::GroupArgs ga{};
-  ga.key = rhs_indices;
-  ga.P = batch;
-  ga.E = E;
-  ga.seg = seg;
-  ga.nseg = (int)nseg;
-  ga.hist = cv.take<int32_t>(nseg * E);
-  ga.segbase = cv.take<int32_t>(nseg * E);
-  ga.offsets = cv.take<int32_t>(E + 1);
-  ga.active = cv.take<int32_t>(E);
-  ga.n_active = cv.take<int32_t>(1);
-  ga.perm = cv.take<uint32_t>(batch);
-  ga.inv = nullptr;
-  MOE_CUDA(ctx, moe::launch_group(ga, ctx->stream));
-
-  moe_qweight m{w, scales, biases};
-  moe::QgemvArgs q = qgemv_args(m, nullptr, (int)N, (int)K);
-  q.x = static_cast<const uint16_t*>(x);
-  q.x_mode = lhs_indices ? 2 : 1;
-  q.x_repeat = (int)std::max<int64_t>(1, x_repeat);
-  q.lhs = lhs_indices;
-  q.perm = ga.perm;
-  q.offsets = ga.offsets;
-  q.active = ga.active;
-  q.n_active = ga.n_active;
-  q.out = static_cast<uint16_t*>(out);
-  q.out_mode = 1;
-  const int slots = (int)std::min<int64_t>(batch, E);
-  MOE_CUDA(ctx, moe::launch_qgemv(q, false, slots, (int)std::min<int64_t>((batch + slots - 1) / slots, 1 << 20), ctx->stream));
+  carve(ctx->scratch, gc.g, gc.status);
+  gc.g.seg = seg;
+  gc.g.nseg = (int)nseg;
+  gc.x = static_cast<const uint16_t*>(x);
+  gc.x_mode = lhs_indices ? 2 : 1;
+  gc.x_repeat = (int)std::max<int64_t>(1, x_repeat);
+  gc.lhs = lhs_indices;
+  gc.w = w;
+  gc.s = static_cast<const uint16_t*>(scales);
+  gc.b = static_cast<const uint16_t*>(biases);
+  gc.E = E;
+  gc.N = (int)N;
+  gc.K = (int)K;
+  gc.batch = batch;
+  gc.rhs = rhs_indices;
+  gc.out = static_cast<uint16_t*>(out);
+  MOE_CUDA(ctx, moe::launch_gather_qmm(gc, ctx->stream));
   return MOE_OK;
 }
 

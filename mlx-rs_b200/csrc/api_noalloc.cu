@@ -14,6 +14,13 @@
 // (the array below is sized for exactly that, 64 KiB per GPU that loads the library,
 // held until the process exits); larger calls are rejected with MOE_ERR_INVALID.
 //
+// Kernels: the same launch sequence as moe_gather_qmm (moe::launch_gather_qmm: the
+// grouping, then the GEMV and, for experts with many rows, the tcgen05 GEMM, with the
+// same per-call choices), so both entry points give bit-identical outputs. The one
+// difference: the tcgen05 kernel gets no status word here, so a bounded wait that
+// expires inside it (a kernel that ended early and left its outputs invalid) is not
+// reported through moe_ctx_status for this entry point.
+//
 // Shared state: every call on a device uses the same array and the array keeps the
 // previous call's contents. Nothing in it needs to start at zero: each grouping kernel
 // writes every element that a later kernel of the same call reads. Calls whose work
@@ -48,19 +55,20 @@ void* g_scratch_ptr[kMaxDevices] = {};
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 struct Layout {
-  size_t hist, segbase, offsets, active, n_active, perm, end;
+  size_t hist, segbase, offsets, active, n_active, tile_start, perm, end;
 };
 
 Layout layout(int64_t batch, int E) {
   const int64_t nseg = std::max<int64_t>(1, (batch + kSeg - 1) / kSeg);
   Layout l{};
   size_t o = 0;
-  l.hist = o;     o = align256(o + sizeof(int32_t) * nseg * E);
-  l.segbase = o;  o = align256(o + sizeof(int32_t) * nseg * E);
-  l.offsets = o;  o = align256(o + sizeof(int32_t) * (E + 1));
-  l.active = o;   o = align256(o + sizeof(int32_t) * E);
-  l.n_active = o; o = align256(o + sizeof(int32_t));
-  l.perm = o;     o = align256(o + sizeof(uint32_t) * batch);
+  l.hist = o;       o = align256(o + sizeof(int32_t) * nseg * E);
+  l.segbase = o;    o = align256(o + sizeof(int32_t) * nseg * E);
+  l.offsets = o;    o = align256(o + sizeof(int32_t) * (E + 1));
+  l.active = o;     o = align256(o + sizeof(int32_t) * E);
+  l.n_active = o;   o = align256(o + sizeof(int32_t));
+  l.tile_start = o; o = align256(o + sizeof(int32_t) * (E + 1));
+  l.perm = o;       o = align256(o + sizeof(uint32_t) * batch);
   l.end = o;
   return l;
 }
@@ -73,7 +81,12 @@ namespace moe_internal {
 int ctx_device(const moe_ctx* ctx);
 void* ctx_stream(const moe_ctx* ctx);
 void ctx_set_error(moe_ctx* ctx, const char* msg);
+int check_gather(moe_ctx* ctx, const char* fn, const void* x, int64_t K, int64_t x_repeat,
+                 const uint32_t* lhs_indices, const uint32_t* w, const void* scales, int64_t num_experts,
+                 int64_t N, const uint32_t* rhs_indices, int64_t batch, int transpose, int group_size, int bits,
+                 const void* out);
 }  // namespace moe_internal
+using moe_internal::check_gather;
 using moe_internal::ctx_device;
 using moe_internal::ctx_set_error;
 using moe_internal::ctx_stream;
@@ -93,6 +106,10 @@ extern "C" int moe_gather_qmm_noalloc(moe_ctx* ctx, const void* x, int64_t x_row
   if (!ctx) return MOE_ERR_INVALID;
   char msg[256];
   ctx_set_error(ctx, "");
+  // the same checks, codes and order as moe_gather_qmm; then the fixed-scratch limits
+  int rc = check_gather(ctx, "moe_gather_qmm_noalloc", x, K, x_repeat, lhs_indices, w, scales, num_experts, N,
+                        rhs_indices, batch, transpose, group_size, bits, out);
+  if (rc || batch == 0) return rc;
   if (batch > MOE_NOALLOC_MAX_BATCH || num_experts > MOE_NOALLOC_MAX_EXPERTS) {
     snprintf(msg, sizeof(msg),
              "moe_gather_qmm_noalloc: batch=%lld / num_experts=%lld exceed the fixed scratch "
@@ -100,25 +117,6 @@ extern "C" int moe_gather_qmm_noalloc(moe_ctx* ctx, const void* x, int64_t x_row
              (long long)batch, (long long)num_experts, MOE_NOALLOC_MAX_BATCH, MOE_NOALLOC_MAX_EXPERTS);
     return noalloc_fail(ctx, MOE_ERR_INVALID, msg);
   }
-  if (bits != 4 || group_size != 64) {
-    snprintf(msg, sizeof(msg), "moe_gather_qmm_noalloc: only bits=4, group_size=64 (got %d, %d)", bits,
-             group_size);
-    return noalloc_fail(ctx, (bits == 2 || bits == 3 || bits == 5 || bits == 6 || bits == 8) &&
-                                     (group_size == 32 || group_size == 64 || group_size == 128)
-                                 ? MOE_ERR_UNSUPPORTED
-                                 : MOE_ERR_INVALID,
-                        msg);
-  }
-  if (!transpose) return noalloc_fail(ctx, MOE_ERR_UNSUPPORTED, "moe_gather_qmm_noalloc: transpose=false");
-  if (K <= 0 || K % 64 != 0 || N <= 0 || N > INT32_MAX || num_experts <= 0 || batch < 0)
-    return noalloc_fail(ctx, MOE_ERR_INVALID, "moe_gather_qmm_noalloc: bad K/N/num_experts/batch");
-  if (!lhs_indices && x_repeat <= 0)
-    return noalloc_fail(ctx, MOE_ERR_INVALID, "moe_gather_qmm_noalloc: x_repeat must be positive");
-  if (batch == 0) return MOE_OK;
-  if (!x || !w || !scales || !rhs_indices || !out)
-    return noalloc_fail(ctx, MOE_ERR_INVALID, "moe_gather_qmm_noalloc: null pointer");
-  if ((reinterpret_cast<uintptr_t>(x) & 15u) || (reinterpret_cast<uintptr_t>(w) & 15u))
-    return noalloc_fail(ctx, MOE_ERR_INVALID, "moe_gather_qmm_noalloc: x and w must be 16-byte aligned");
 
   const int dev = ctx_device(ctx);
   if (dev < 0 || dev >= kMaxDevices) return noalloc_fail(ctx, MOE_ERR_INVALID, "moe_gather_qmm_noalloc: device");
@@ -126,7 +124,6 @@ extern "C" int moe_gather_qmm_noalloc(moe_ctx* ctx, const void* x, int64_t x_row
   if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
   if (prev != dev && cudaSetDevice(dev) != cudaSuccess)
     return noalloc_fail(ctx, MOE_ERR_CUDA, "moe_gather_qmm_noalloc: cudaSetDevice failed");
-  int rc = MOE_OK;
   void* base = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_mu);
@@ -151,40 +148,31 @@ extern "C" int moe_gather_qmm_noalloc(moe_ctx* ctx, const void* x, int64_t x_row
       return noalloc_fail(ctx, MOE_ERR_INVALID, "moe_gather_qmm_noalloc: fixed scratch too small");
     }
     char* s = static_cast<char*>(base);
-    cudaStream_t st = static_cast<cudaStream_t>(ctx_stream(ctx));
-    moe::GroupArgs ga{};
-    ga.key = rhs_indices;
-    ga.P = batch;
-    ga.E = E;
-    ga.seg = kSeg;
-    ga.nseg = (int)std::max<int64_t>(1, (batch + kSeg - 1) / kSeg);
-    ga.hist = reinterpret_cast<int32_t*>(s + l.hist);
-    ga.segbase = reinterpret_cast<int32_t*>(s + l.segbase);
-    ga.offsets = reinterpret_cast<int32_t*>(s + l.offsets);
-    ga.active = reinterpret_cast<int32_t*>(s + l.active);
-    ga.n_active = reinterpret_cast<int32_t*>(s + l.n_active);
-    ga.perm = reinterpret_cast<uint32_t*>(s + l.perm);
-    ga.inv = nullptr;
-    cudaError_t e = moe::launch_group(ga, st);
-    if (e == cudaSuccess) {
-      moe::QgemvArgs q{};
-      q.x = static_cast<const uint16_t*>(x);
-      q.x_mode = lhs_indices ? 2 : 1;
-      q.x_repeat = (int)std::max<int64_t>(1, x_repeat);
-      q.lhs = lhs_indices;
-      q.perm = ga.perm;
-      q.offsets = ga.offsets;
-      q.active = ga.active;
-      q.n_active = ga.n_active;
-      q.w0 = w;
-      q.s0 = static_cast<const uint16_t*>(scales);
-      q.b0 = static_cast<const uint16_t*>(biases);
-      q.N = (int)N;
-      q.K = (int)K;
-      q.out = static_cast<uint16_t*>(out);
-      q.out_mode = 1;
-      e = moe::launch_qgemv(q, false, (int)std::min<int64_t>(batch, E), (int)std::min<int64_t>(batch, 16), st);
-    }
+    moe::GatherCall gc{};
+    gc.g.seg = kSeg;
+    gc.g.nseg = (int)std::max<int64_t>(1, (batch + kSeg - 1) / kSeg);
+    gc.g.hist = reinterpret_cast<int32_t*>(s + l.hist);
+    gc.g.segbase = reinterpret_cast<int32_t*>(s + l.segbase);
+    gc.g.offsets = reinterpret_cast<int32_t*>(s + l.offsets);
+    gc.g.active = reinterpret_cast<int32_t*>(s + l.active);
+    gc.g.n_active = reinterpret_cast<int32_t*>(s + l.n_active);
+    gc.g.tile_start = reinterpret_cast<int32_t*>(s + l.tile_start);
+    gc.g.perm = reinterpret_cast<uint32_t*>(s + l.perm);
+    gc.status = nullptr;  // no status word: see the header comment
+    gc.x = static_cast<const uint16_t*>(x);
+    gc.x_mode = lhs_indices ? 2 : 1;
+    gc.x_repeat = (int)std::max<int64_t>(1, x_repeat);
+    gc.lhs = lhs_indices;
+    gc.w = w;
+    gc.s = static_cast<const uint16_t*>(scales);
+    gc.b = static_cast<const uint16_t*>(biases);
+    gc.E = E;
+    gc.N = (int)N;
+    gc.K = (int)K;
+    gc.batch = batch;
+    gc.rhs = rhs_indices;
+    gc.out = static_cast<uint16_t*>(out);
+    const cudaError_t e = moe::launch_gather_qmm(gc, static_cast<cudaStream_t>(ctx_stream(ctx)));
     if (e != cudaSuccess) {
       snprintf(msg, sizeof(msg), "moe_gather_qmm_noalloc: launch failed: %s", cudaGetErrorString(e));
       rc = noalloc_fail(ctx, MOE_ERR_CUDA, msg);
@@ -194,7 +182,7 @@ extern "C" int moe_gather_qmm_noalloc(moe_ctx* ctx, const void* x, int64_t x_row
   return rc;
 }
 
-static_assert(sizeof(int32_t) * 4 * MOE_NOALLOC_MAX_EXPERTS * 2 + sizeof(int32_t) * (2 * MOE_NOALLOC_MAX_EXPERTS + 2) +
-                      sizeof(uint32_t) * MOE_NOALLOC_MAX_BATCH + 6 * 256 <=
+static_assert(sizeof(int32_t) * 4 * MOE_NOALLOC_MAX_EXPERTS * 2 + sizeof(int32_t) * (3 * MOE_NOALLOC_MAX_EXPERTS + 3) +
+                      sizeof(uint32_t) * MOE_NOALLOC_MAX_BATCH + 7 * 256 <=
                   kScratchBytes,
               "fixed scratch too small for the stated limits");

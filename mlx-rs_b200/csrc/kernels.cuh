@@ -160,6 +160,28 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, bool gated, cudaStream_t st);
 
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st);
 
+// One gather_qmm (out[i] = x[row(i)] . dequant(w[rhs[i]])^T, out in the caller's row
+// order): grouping by expert, then each expert on the kernel its row count calls for
+// (tcgen05 for experts with many rows, the GEMV for the rest), as in the block. The
+// scratch pointers of g (hist, segbase, offsets, active, n_active, perm, tile_start,
+// seg, nseg) and status come from the caller; the rest of g is filled here.
+struct GatherCall {
+  const uint16_t* x;
+  int x_mode;  // 1: x row = i / x_repeat, 2: x row = lhs[i]
+  int x_repeat;
+  const uint32_t* lhs;
+  const uint32_t* w;
+  const uint16_t* s;
+  const uint16_t* b;
+  int E, N, K;
+  int64_t batch;
+  const uint32_t* rhs;
+  uint16_t* out;
+  GroupArgs g;
+  int32_t* status;
+};
+cudaError_t launch_gather_qmm(const GatherCall& c, cudaStream_t st);
+
 // Expert parallelism. Partial combine of one rank's experts [e0, e0 + E_l):
 // partial[t, :] (fp32) = sum over j = 0..k-1 in order, of the pairs p = t*k + j whose
 // expert is local, of bf16(y[inv[p], :] * weight_p); zero for tokens with none.

@@ -537,6 +537,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
   __syncthreads();
   if (abort_flag && tid == 0 && ta.status) atomicOr(ta.status, abort_flag);
   if (warp == kMmaWarp) {
+    // Every MMA this CTA issued has completed before its tensor memory is freed: the
+    // issuer commits bar_done after its last MMA on every path, including after a
+    // producer or the issuer gave up waiting (the epilogue then skipped its own wait).
+    if (lane == 0 && !mbar_wait(bar_done, 0) && ta.status) atomicOr(ta.status, 8);
+    __syncwarp();
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(C::kTmemCols) : "memory");
   }

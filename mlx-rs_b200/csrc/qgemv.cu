@@ -805,7 +805,9 @@ __global__ void __launch_bounds__(512) qgemv_i8_kernel(QgemvArgs a, int units_pe
         sh = 13 - (ex < -126 ? -126 : ex);
         sh = sh > 126 ? 126 : sh;
       }
-      const float us = __int_as_float((127 - sh) << 23);  // 2^-sh, sh in [-114, 126]
+      // 2^-sh, sh in [-114, 126]; a token row holding inf or NaN has no fixed-point form
+      // (its limbs saturated): its outputs become NaN, as the bf16 kernel's would
+      const float us = mb >= 0x7f80 ? __int_as_float(0x7fc00000) : __int_as_float((127 - sh) << 23);
       const int64_t pos = cbase + tok;
       const int64_t orow = a.out_mode == 0 ? pos : rm.orig(pos);
       uint16_t* o = a.out + (size_t)orow * N;
