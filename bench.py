@@ -69,6 +69,8 @@ def parse():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the per-configuration sub-records of the default run")
     return ap.parse_args()
 
 
@@ -169,6 +171,42 @@ def make_workload(args, S, host=True):
     return cfg, bw, T, regime, layers
 
 
+def workload_config(cfg, regime, T, world, layers, tokens_per_gpu=None):
+    """The `config` object of a bench line: the same dict in both arms (b200 and
+    reference) for the same workload and GPU count."""
+    what = f"stack of {layers} MoE blocks + RMSNorm" if layers > 1 else "MoE block"
+    per = "in total" if layers > 1 else "per GPU"
+    c = {"workload": f"{cfg.name} {what} {regime}, T={T} tokens {per}",
+         "global_batch": T * (world if layers == 1 else 1), "seq_len": 1,
+         "parallelism": f"ep{world}" if world > 1 else "single",
+         "experts": cfg.num_experts, "top_k": cfg.top_k, "hidden": cfg.hidden, "moe_inter": cfg.moe_inter,
+         "shared_inter": cfg.shared_inter,
+         "l2": ("inputs larger than L2 (each step streams every block's weights)" if layers > 1
+                else "flushed (256 MiB write) before every timed step")}
+    if tokens_per_gpu is not None:
+        c["tokens_per_gpu"] = tokens_per_gpu
+    return c
+
+
+def parity_metrics(y_bits, ref_bits):
+    """Output parity of GPU rows against the oracle's rows for the same tokens (bf16 bit
+    patterns): max |diff|, max |diff| / rms(ref), mean relative error, max error in bf16
+    ulps of the reference value, share of bit-identical elements."""
+    import numpy as np
+
+    def f(b):
+        return (np.asarray(b, np.uint16).astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    y, r = f(y_bits), f(ref_bits)
+    d = np.abs(y - r)
+    rms = float(np.sqrt(np.mean(r * r)))
+    ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(r), 2.0 ** -126))) - 7)
+    return {"max_abs": float(d.max()), "max_abs_over_rms": float(d.max() / rms) if rms else 0.0,
+            "mean_rel": float(d.mean() / np.mean(np.abs(r))) if np.any(r) else 0.0,
+            "max_ulp": float((d / ulp).max()), "frac_exact": float(np.mean(d == 0)), "rms_ref": rms,
+            "tolerance": "mean_rel <= 1e-2 and |diff| <= 2e-2 + 2 (GEMV) or 4 (tcgen05) bf16 ulps of the row's "
+                         "largest |value|", "rows": int(np.asarray(ref_bits).shape[0])}
+
+
 def reference_arm(args):
     """The CPU oracle on this host's cores (rank 0 only)."""
     rank = int(os.environ.get("RANK", "0"))
@@ -194,13 +232,11 @@ def reference_arm(args):
         times.append(time.perf_counter() - t0)
     ms = 1e3 * statistics.mean(times) * layers
     value = Ts / (ms / 1e3)
-    what = f"{layers}-block stack" if layers > 1 else "MoE block"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong" if layers > 1 else "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"{cfg.name} {what} {regime}, T={T} tokens", "global_batch": T,
-                   "parallelism": "cpu"},
+        "config": workload_config(cfg, regime, T, world, layers, T // world if layers > 1 else None),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"{args.steps} block calls of {Ts} of the T={T} tokens (CPU oracle, C "
                                    f"restatement of the reference block; MLX itself is not available)"
@@ -210,23 +246,31 @@ def reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
-def cpu_baseline(bw_host, x_host, seconds):
+def cpu_baseline(bw_host, x_host, seconds, gpu_rows=None):
+    """The CPU oracle on this host's cores over the sample x_host (median time of up to
+    20 calls within `seconds`). With gpu_rows (the GPU block's output rows for the same
+    tokens), the oracle's output of the sample is also the parity reference: adds
+    "parity" (parity_metrics) to the record."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     cores = os.cpu_count() or 1
     T = x_host.shape[0]
     times = []
     t_end = time.perf_counter() + seconds
+    y = None
     while True:
         t0 = time.perf_counter()
-        O.block_forward(bw_host, x_host, nthreads=cores)
+        y, _, _ = O.block_forward(bw_host, x_host, nthreads=cores)
         times.append(time.perf_counter() - t0)
         if time.perf_counter() > t_end or len(times) >= 20:
             break
     ms = 1e3 * statistics.median(times)
-    return {"value": T / (ms / 1e3), "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{len(times)} block calls of T={T} tokens on the CPU oracle (C restatement of the "
-                      f"reference block), median"}
+    r = {"value": T / (ms / 1e3), "unit": "tokens/s", "cores": cores, "kind": "port",
+         "sample": f"{len(times)} block calls of T={T} tokens on the CPU oracle (C restatement of the "
+                   f"reference block), median"}
+    if gpu_rows is not None:
+        r["parity"] = parity_metrics(gpu_rows, y)
+    return r
 
 
 class Timer:
@@ -421,6 +465,119 @@ def main():
             dist.destroy_process_group()
 
 
+# Sub-records of the default run: every benchmark configuration that fits one GPU, as
+# (label, workload, tokens). The headline line is the Qwen3-30B-A3B decode block at T=64.
+CONFIG_RECORDS = [
+    ("C0 Qwen1.5-MoE-A2.7B decode T=1", "qwen15-decode", 1),
+    ("C0 Qwen1.5-MoE-A2.7B prefill T=512", "qwen15-prefill", 512),
+    ("C1 Qwen3-30B-A3B decode T=1", "decode", 1),
+    ("C1 Qwen3-30B-A3B decode T=8", "decode", 8),
+    ("C1 Qwen3-30B-A3B decode T=32", "decode", 32),
+    ("C2 Qwen3-30B-A3B prefill T=4096, uniform routing", "prefill", 4096),
+    ("C2 Qwen3-30B-A3B prefill T=4096, skewed routing", "prefill-skewed", 4096),
+    ("C3 LFM2-8B-A1B decode T=1", "lfm2-decode", 1),
+    ("C3 LFM2-8B-A1B prefill T=1024", "lfm2-prefill", 1024),
+]
+
+
+def block_roofline(cfg, regime, T, stage_ms, U, ms):
+    """Roofline of one block run: the dominant expert kernel (decode: algorithmic bytes
+    of the distinct experts selected ÷ its device time, against HBM; prefill: 2·P·N·K ÷
+    its device time, against the bf16 burst peak) and the whole block's fraction."""
+    H, I, k = cfg.hidden, cfg.moe_inter, cfg.top_k
+    import mlx_rs_b200.synth as S
+    wb = S.weight_bytes(cfg)
+    per_mat = wb["per_expert"] / 3
+    P = T * k
+    alg = {"gate_up": U * 2 * per_mat + T * H * 2, "down": U * per_mat + P * I * 2}
+    flops = {"gate_up": 2.0 * P * 2 * H * I, "down": 2.0 * P * H * I}
+    shared_flops = 2.0 * T * 3 * H * cfg.shared_inter
+    dom = max(("gate_up", "down"), key=lambda kk: stage_ms[kk])
+    block_bytes = alg["gate_up"] + alg["down"] + wb["router"] + wb["shared"] + T * H * 2
+    block_flops = flops["gate_up"] + flops["down"] + 2.0 * T * cfg.num_experts * H + shared_flops
+    hbm, tf, _ = measured_peaks()
+    extra = {"stage_ms": stage_ms, "block_ms": ms,
+             "block_algorithmic_GBps": block_bytes / (ms / 1e3) / 1e9,
+             "block_hbm_frac": block_bytes / (ms / 1e3) / 1e9 / hbm,
+             "block_TFLOPs": block_flops / (ms / 1e3) / 1e12,
+             "block_tensor_frac": block_flops / (ms / 1e3) / 1e12 / tf}
+    if regime == "prefill":
+        kind = "tcgen05 grouped GEMM" if P >= 32 * cfg.num_experts else "qgemv"
+        return tensor_roofline(f"{kind} {dom}", flops[dom], stage_ms[dom], extra)
+    return hbm_roofline(f"qgemv {dom}", alg[dom], stage_ms[dom], extra)
+
+
+def config_records(args, dev, flush, cpu_seconds=2.0):
+    """One record per CONFIG_RECORDS entry: tokens/s of the block replayed from a CUDA
+    graph (CUDA events around each replay, L2 flushed before each), the roofline of its
+    dominant kernel and of the whole block, the CPU oracle on a token sample, and the
+    parity of the GPU rows of that sample against the oracle's."""
+    import torch
+
+    import mlx_rs_b200.synth as S
+    from mlx_rs_b200.block import SparseMoeBlock
+
+    recs = []
+    stream = torch.cuda.current_stream(dev)
+    cache = {}
+    for label, wl, T in CONFIG_RECORDS:
+        sub = argparse.Namespace(**vars(args))
+        sub.workload, sub.tokens = wl, T
+        key = WORKLOADS[wl][:5]
+        if key not in cache:
+            cache.clear()
+            torch.cuda.empty_cache()
+            cfg, bw_host, _, regime, _ = make_workload(sub, S)
+            cache[key] = (cfg, bw_host, SparseMoeBlock(S.to_device(bw_host, dev), cfg))
+        cfg, bw_host, blk = cache[key]
+        regime = WORKLOADS[wl][5]
+        H = cfg.hidden
+        xs_host = [S.host_x(2000 + i, T, H) for i in range(4)]
+        xs = [S.x_to_device(x, dev) for x in xs_host]
+        blk.reserve(T)
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        static_x = xs[0].clone()
+        for i in range(3):
+            blk.forward(xs[i % 4], out)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            blk.forward(static_x, out)
+        times = []
+        for i in range(max(3, args.warmup) + args.steps):
+            static_x.copy_(xs[i % 4])
+            flush.zero_()
+            a, b = events()
+            a.record(stream)
+            g.replay()
+            b.record(stream)
+            if i >= max(3, args.warmup):
+                times.append((a, b))
+        torch.cuda.synchronize()
+        ms = statistics.mean(a.elapsed_time(b) for a, b in times)
+        del g
+        stage_acc, n_act = {}, []
+        for i in range(4):
+            flush.zero_()
+            _, st, na = blk.profile(xs[i % 4], out)
+            n_act.append(na)
+            for kk, v in st.items():
+                stage_acc.setdefault(kk, []).append(v)
+        stage_ms = {kk: statistics.mean(v) for kk, v in stage_acc.items()}
+        roof = block_roofline(cfg, regime, T, stage_ms, statistics.mean(n_act), ms)
+        n_s = min(T, 32)
+        gpu_rows = S.bf16_tensor_to_bits(blk.forward(xs[0], out)[:n_s])
+        cpu = cpu_baseline(bw_host, xs_host[0][:n_s], cpu_seconds, gpu_rows)
+        if T > n_s:
+            cpu["sample"] += f" ({n_s} of the {T} tokens; rows are independent)"
+        recs.append({"config": label, "workload": wl, "tokens": T, "value": T / (ms / 1e3), "unit": "tokens/s",
+                     "ms_per_step": ms, "launch": "cuda_graph", "distinct_experts": statistics.mean(n_act),
+                     "roofline": roof, "parity": cpu.pop("parity"), "cpu_baseline": cpu})
+    cache.clear()
+    torch.cuda.empty_cache()
+    return recs
+
+
 def run_block(args, dev):
     """One GPU, one block: device time from a CUDA graph, stage profile, e2e, sweep."""
     import numpy as np
@@ -560,22 +717,29 @@ def run_block(args, dev):
                                "stage_us": {kk: round(vv * 1e3, 2) for kk, vv in st.items()},
                                "block_GBps": bytes_ / (statistics.median(tms) / 1e3) / 1e9}
 
-    cpu = cpu_baseline(bw_host, xs_host[0][: min(T, 128)], args.cpu_seconds)
+    n_s = min(T, 128)
+    gpu_rows = S.bf16_tensor_to_bits(blk.forward(xs[0], out)[:n_s])
+    cpu = cpu_baseline(bw_host, xs_host[0][:n_s], args.cpu_seconds, gpu_rows)
     if T > 128:
-        cpu["sample"] += f" ({min(T, 128)} of the {T} tokens; rows are independent)"
+        cpu["sample"] += f" ({n_s} of the {T} tokens; rows are independent)"
     launches = 5 + group_launches(P, cfg.num_experts) + (2 if cfg.shared_inter else 0)
+    configs = []
+    if args.workload == "decode" and not args.tokens and not args.no_configs:
+        del bw_host
+        configs = config_records(args, dev, flush)
     return {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"{cfg.name} MoE block {regime}, T={T} tokens per GPU", "global_batch": T,
-                   "seq_len": 1, "parallelism": "single",
-                   "experts": cfg.num_experts, "top_k": cfg.top_k, "hidden": H, "moe_inter": cfg.moe_inter,
-                   "l2": "flushed (256 MiB write) before every timed step", "launch": mode,
-                   "clock_window": "nvidia-smi every 200 ms across 0.6 s of untimed steps, the timed steps, 0.6 s more",
-                   "distinct_experts_per_step": U, "sweep_eager": sweep},
+        "config": workload_config(cfg, regime, T, 1, 1),
+        "details": {"launch": mode,
+                    "clock_window": "nvidia-smi every 200 ms across 0.6 s of untimed steps, the timed steps, "
+                                    "0.6 s more",
+                    "distinct_experts_per_step": U, "sweep_eager": sweep},
         "roofline": roof,
+        "parity": cpu.get("parity"),
         "cpu_baseline": cpu,
+        "configs": configs,
         "e2e": {"value": T / (e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
                 "d2h_bytes_per_step": T * H * 2, "ms_per_step": e2e, "api": e2e_api},
         "gpu_launches": launches * args.steps,
@@ -681,12 +845,11 @@ def run_ep_block(args, world, rank, local, dev):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"{cfg.name} MoE block {regime}, T={T} tokens per GPU, expert-parallel",
-                   "global_batch": T * world, "seq_len": 1, "parallelism": f"ep{world}",
-                   "experts": cfg.num_experts, "experts_per_gpu": n, "top_k": cfg.top_k, "hidden": H,
-                   "moe_inter": cfg.moe_inter, "collectives": "NCCL all_gather x2 (dispatch), all_to_all (combine)",
-                   "l2": "flushed (256 MiB write) before every timed step", "launch": mode,
-                   "clock_window": "nvidia-smi every 200 ms across 0.6 s of untimed steps, the timed steps, 0.6 s more"},
+        "config": workload_config(cfg, regime, T, world, 1),
+        "details": {"experts_per_gpu": n, "collectives": "NCCL all_gather x2 (dispatch), all_to_all (combine)",
+                    "launch": mode,
+                    "clock_window": "nvidia-smi every 200 ms across 0.6 s of untimed steps, the timed steps, "
+                                    "0.6 s more"},
         "roofline": roof,
         "cpu_baseline": None,
         "e2e": {"value": world * T / (e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
@@ -800,11 +963,10 @@ def run_stack(args, world, rank, local, dev):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"{cfg.name} stack of {layers} MoE blocks + RMSNorm, {regime}, T={T} tokens in total",
-                   "global_batch": T, "tokens_per_gpu": T_r, "seq_len": 1,
-                   "parallelism": f"ep{world}" if world > 1 else "single", "experts_per_gpu": n,
-                   "l2": "inputs larger than L2 (each step streams every block's weights)", "launch": mode,
-                   "clock_window": "nvidia-smi every 200 ms across 0.6 s of untimed steps, the timed steps, 0.6 s more"},
+        "config": workload_config(cfg, regime, T, world, layers, T_r),
+        "details": {"experts_per_gpu": n, "launch": mode,
+                    "clock_window": "nvidia-smi every 200 ms across 0.6 s of untimed steps, the timed steps, "
+                                    "0.6 s more"},
         "roofline": roof,
         "cpu_baseline": cpu,
         "e2e": {"value": T / (e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T_r * H * 2,

@@ -22,3 +22,22 @@ def test_reference_arm_prints_one_contract_line():
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"]["value"] == d["value"] and d["e2e"]["h2d_bytes_per_step"] == 0
     assert d["config"]["workload"].startswith("qwen3-30b-a3b")
+
+
+def test_reference_arm_config_equals_gpu_arm_config():
+    """Both arms describe the default workload with the same `config` object (the GPU
+    arm builds it with the same function from the same workload table)."""
+    import argparse
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    import mlx_rs_b200.synth as S
+    args = argparse.Namespace(workload="decode", tokens=None)
+    cfg, _, T, regime, layers = bench.make_workload(args, S, host=False)
+    want = bench.workload_config(cfg, regime, T, 1, layers)
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
+                        "--warmup", "1"], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    d = json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][0])
+    assert d["config"] == want
+    assert [c[1] for c in bench.CONFIG_RECORDS if c[1] in bench.WORKLOADS] == [c[1] for c in bench.CONFIG_RECORDS]
