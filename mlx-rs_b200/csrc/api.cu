@@ -351,6 +351,37 @@ bool fused_route_enabled() {
 // Routing + grouping of one block call into ws.
 // With `packed`, routing writes [T, k] expert | bf16(weight) << 16 there and stops
 // before the grouping (the expert-parallel route).
+// Router and top-k arguments of a block call (logits into ws.logits).
+void route_args(const moe_block_config* c, const moe_block_weights* w, const void* x, int64_t T, const BlockWs& ws,
+                moe::RouterArgs& ra, moe::TopkArgs& ta) {
+  const int E = c->num_experts;
+  const bool gate_row = c->shared_inter > 0 && c->has_shared_gate;
+  ra = moe::RouterArgs{};
+  ra.x = static_cast<const uint16_t*>(x);
+  ra.T = (int)T;
+  ra.K = c->hidden;
+  ra.E = E;
+  ra.n_rows = E + (gate_row ? 1 : 0);
+  ra.group_size = c->group_size;
+  ra.w = w->router.w;
+  ra.s = static_cast<const uint16_t*>(w->router.scales);
+  ra.b = static_cast<const uint16_t*>(w->router.biases);
+  ra.gate_w = w->shared_expert_gate.w;
+  ra.gate_s = static_cast<const uint16_t*>(w->shared_expert_gate.scales);
+  ra.gate_b = static_cast<const uint16_t*>(w->shared_expert_gate.biases);
+  ra.logits = ws.logits;
+  ta = moe::TopkArgs{};
+  ta.logits = ws.logits;
+  ta.T = (int)T;
+  ta.E = E;
+  ta.n_rows = ra.n_rows;
+  ta.k = c->top_k;
+  ta.scoring = c->scoring;
+  ta.norm_topk_prob = c->norm_topk_prob;
+  ta.expert_bias = static_cast<const uint16_t*>(w->expert_bias);
+  ta.gate_val = gate_row ? ws.gate_val : nullptr;
+}
+
 int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* w, const void* x, int64_t T,
               const BlockWs& ws, cudaEvent_t* ev = nullptr, uint32_t* packed = nullptr, int tc_min_rows = 0) {
   const int E = c->num_experts;
@@ -418,6 +449,32 @@ int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* 
   MOE_MARK(ev, kGroup, ctx->stream);
   MOE_CUDA(ctx, moe::launch_group(ga, ctx->stream));
   return MOE_OK;
+}
+
+// Decode-sized batches (T <= 8 tokens, T * k <= 64 pairs) run the whole block in one
+// cooperative kernel when the shapes fit its shared memory and every scale / bias array
+// is 4-byte aligned; MOE_B200_DECODE=0 in the environment keeps the launch chain.
+constexpr int kDecodeBarrierWord = 60;  // grid barrier word of the decode kernel, in the status block
+static_assert(kDecodeBarrierWord >= kFusedCounterWord + moe::kFusedRouteCounters && kDecodeBarrierWord < 64,
+              "status block");
+bool decode_fused_ok(const moe_block_config* c, const moe_block_weights* w, int64_t T) {
+  const char* v = std::getenv("MOE_B200_DECODE");
+  if (v && v[0] == '0') return false;
+  if (T > moe::kDecodeMaxT || !moe::decode_smem_bytes((int)T, c->top_k, c->hidden, c->moe_inter, c->shared_inter))
+    return false;
+  const moe_qweight* m[6] = {&w->gate, &w->up, &w->down, &w->shared_gate, &w->shared_up, &w->shared_down};
+  for (int i = 0; i < (c->shared_inter > 0 ? 6 : 3); ++i)
+    if ((reinterpret_cast<uintptr_t>(m[i]->scales) | reinterpret_cast<uintptr_t>(m[i]->biases)) & 3) return false;
+  return true;
+}
+// 1 when every scale / bias row of every projection moves as 8-byte pieces (groups per
+// row a multiple of 4, arrays 8-byte aligned); else the kernel copies 4 bytes at a time.
+int decode_scale8(const moe_block_config* c, const moe_block_weights* w) {
+  if ((c->hidden / 64) % 4 || (c->moe_inter / 64) % 4 || (c->shared_inter / 64) % 4) return 0;
+  const moe_qweight* m[6] = {&w->gate, &w->up, &w->down, &w->shared_gate, &w->shared_up, &w->shared_down};
+  for (int i = 0; i < (c->shared_inter > 0 ? 6 : 3); ++i)
+    if ((reinterpret_cast<uintptr_t>(m[i]->scales) | reinterpret_cast<uintptr_t>(m[i]->biases)) & 7) return 0;
+  return 1;
 }
 
 // Tensor-core (tcgen05) GEMM for many rows per expert, GEMV (mma.sync) for few.
@@ -570,6 +627,42 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   BlockWs ws = carve_block(ctx->scratch, cfg, T);
   const int E = cfg->num_experts, H = cfg->hidden, I = cfg->moe_inter, k = cfg->top_k;
   const int64_t P = T * k;
+  if (decode_fused_ok(cfg, wts, T)) {
+    // decode-sized batch: the whole block in one cooperative kernel (decode.cu); under
+    // moe_block_profile its time is booked as the gate/up stage
+    moe::DecodeArgs d{};
+    route_args(cfg, wts, x, T, ws, d.ra, d.ta);
+    d.T = (int)T;
+    d.H = H;
+    d.I = I;
+    d.Is = cfg->shared_inter;
+    d.k = k;
+    auto q = [](const moe_qweight& m, const uint32_t*& w, const uint16_t*& s, const uint16_t*& b) {
+      w = m.w;
+      s = static_cast<const uint16_t*>(m.scales);
+      b = static_cast<const uint16_t*>(m.biases);
+    };
+    q(wts->gate, d.wg, d.sg, d.bg);
+    q(wts->up, d.wu, d.su, d.bu);
+    q(wts->down, d.wd, d.sd, d.bd);
+    if (d.Is) {
+      q(wts->shared_gate, d.swg, d.ssg, d.sbg);
+      q(wts->shared_up, d.swu, d.ssu, d.sbu);
+      q(wts->shared_down, d.swd, d.ssd, d.sbd);
+    }
+    d.hbuf = ws.hbuf;
+    d.hsbuf = ws.hs;
+    d.residual = static_cast<const uint16_t*>(residual);
+    d.out = static_cast<uint16_t*>(out);
+    d.barrier = reinterpret_cast<uint32_t*>(ws.status) + kDecodeBarrierWord;
+    d.status = ws.status;
+    d.has_gate = cfg->shared_inter > 0 && cfg->has_shared_gate;
+    d.scale8 = decode_scale8(cfg, wts);
+    for (int i = kRouter; i <= kGateUp; ++i) MOE_MARK(ev, i, ctx->stream);
+    MOE_CUDA(ctx, moe::launch_decode_block(d, ctx->stream));
+    for (int i = kDown; i <= kStages; ++i) MOE_MARK(ev, i, ctx->stream);
+    return MOE_OK;
+  }
   const ExpertPlan plan = plan_experts(P, E, I, H);
   rc = run_route(ctx, cfg, wts, x, T, ws, ev, nullptr, plan.min_rows);
   if (rc) return rc;

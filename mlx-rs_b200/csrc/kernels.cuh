@@ -160,6 +160,38 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, bool gated, cudaStream_t st);
 
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st);
 
+// The whole block for decode-sized batches (T <= kDecodeMaxT tokens) in one persistent
+// cooperative kernel (decode.cu): router logits -> grid barrier -> top-k and grouping
+// (every CTA, in shared memory) -> gate/up + SwiGLU of the selected experts and the
+// shared expert (down weights prefetched into L2 meanwhile) -> grid barrier -> down
+// projection and weighted combine (+ gated shared expert, + residual) per tile of 16
+// hidden rows.
+constexpr int kDecodeMaxT = 8;
+constexpr int kDecodeMaxP = 64;
+constexpr int kDecodeWarps = 8;
+struct DecodeArgs {
+  RouterArgs ra;             // logits into scratch [T, n_rows]
+  TopkArgs ta;               // scoring / top-k / renorm options (output pointers unused)
+  int T, H, I, Is, k;
+  const uint32_t* wg; const uint16_t* sg; const uint16_t* bg;   // gate [E, I, H/8]
+  const uint32_t* wu; const uint16_t* su; const uint16_t* bu;   // up   [E, I, H/8]
+  const uint32_t* wd; const uint16_t* sd; const uint16_t* bd;   // down [E, H, I/8]
+  const uint32_t* swg; const uint16_t* ssg; const uint16_t* sbg;  // shared gate [Is, H/8]
+  const uint32_t* swu; const uint16_t* ssu; const uint16_t* sbu;  // shared up   [Is, H/8]
+  const uint32_t* swd; const uint16_t* ssd; const uint16_t* sbd;  // shared down [H, Is/8]
+  uint16_t* hbuf;            // [T*k, I] scratch (pair order)
+  uint16_t* hsbuf;           // [T, Is] scratch
+  const uint16_t* residual;  // [T, H] added last, or null
+  uint16_t* out;             // [T, H]
+  uint32_t* barrier;         // grid barrier word (any value; left consistent after each call)
+  int32_t* status;           // device status word (bounded waits)
+  int has_gate;              // the shared expert is gated by sigmoid(logit row E)
+  int scale8;                // 1: every scale/bias row pair of 4 groups is one 8-byte copy
+};
+// Dynamic shared memory of the decode kernel (0: the shapes do not fit it).
+size_t decode_smem_bytes(int T, int k, int H, int I, int Is);
+cudaError_t launch_decode_block(const DecodeArgs& a, cudaStream_t st);
+
 // One gather_qmm (out[i] = x[row(i)] . dequant(w[rhs[i]])^T, out in the caller's row
 // order): grouping by expert, then each expert on the kernel its row count calls for
 // (tcgen05 for experts with many rows, the GEMV for the rest), as in the block. The

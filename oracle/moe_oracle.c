@@ -441,7 +441,9 @@ int oracle_softmax_rows(const uint16_t* logits, int64_t rows, int64_t n, uint16_
  * host validator uses (sort_top_pairs / select_top_k, qwen3_moe_python_port.rs:89-93,
  * 491-510; lfm2_moe_python_port.rs:595). The returned set is what
  * argpartition(-p, k-1)[:, :k] (Qwen, :438-440) or argpartition(p, E-k)[:, E-k:]
- * (LFM2, :579-583) selects; indices are listed in that same order.
+ * (LFM2, :579-583) selects; indices are listed in that same order. NaN keys (a
+ * token with a non-finite activation) rank after every other key, by index among
+ * themselves.
  */
 static void topk_row(const uint16_t* key, int64_t E, int k, uint32_t* sel) {
     for (int j = 0; j < k; ++j) {
@@ -453,7 +455,10 @@ static void topk_row(const uint16_t* key, int64_t E, int k, uint32_t* sel) {
                 if (sel[jj] == (uint32_t)e) taken = 1;
             if (taken) continue;
             const float v = bf2f(key[e]);
-            if (best < 0 || v > bv) {
+            /* NaN keys rank after every other key, NaN among NaN by index (e ascends,
+             * so an earlier NaN is kept): a total order, k distinct valid indices */
+            const int better = best < 0 || (isnan(bv) && !isnan(v)) || (!isnan(v) && v > bv);
+            if (better) {
                 best = e;
                 bv = v;
             }

@@ -555,3 +555,49 @@ def test_graphed_block_and_layer_replays_vs_oracle(cfg_name, seed, T):
         yl, _, _, _ = O.layer_ffn_forward(bw, x, nw, 1e-6)
         assert_close(got.reshape(yl.shape), yl, f"{cfg_name} T={T} graphed layer replay {i}")
     torch.cuda.synchronize()
+
+
+# ----------------------------------------------------------------------------------
+# the fused decode kernel (T <= 8: the whole block in one cooperative launch)
+# ----------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("cfg_name,seed", [("QWEN3_30B_A3B", 1), ("QWEN15_MOE_A27B", 0), ("LFM2_8B_A1B", 3)])
+def test_decode_kernel_matches_launch_chain_and_oracle(cfg_name, seed, monkeypatch):
+    """For every T up to 8: the one-launch decode kernel against the oracle (routing of
+    the launch chain bit-exact, outputs within tolerance) and against the launch chain
+    (MOE_B200_DECODE=0), on repeated calls (the grid barrier word is reused without a
+    reset); moe_block_profile reports no expired wait."""
+    import oracle as O
+    from gpu_util import run_block, to_dev
+    cfg = getattr(S, cfg_name)
+    bw, blk = _block(cfg, seed)
+    for T in (1, 2, 3, 5, 8):
+        x = S.host_x(1500 + T, T, cfg.hidden)
+        monkeypatch.setenv("MOE_B200_DECODE", "0")
+        ref = run_block(blk, x)
+        monkeypatch.setenv("MOE_B200_DECODE", "1")
+        got = run_block(blk, x)
+        again = run_block(blk, x)
+        assert np.array_equal(got[0], again[0]), (cfg_name, T)
+        y, idx, w = O.block_forward(bw, x)
+        assert np.array_equal(got[1].reshape(idx.shape), idx)
+        assert_close(got[0].reshape(T, -1), y, f"{cfg_name} T={T} decode kernel vs oracle")
+        assert_close(got[0].reshape(T, -1), ref[0].reshape(T, -1), f"{cfg_name} T={T} decode kernel vs chain")
+        _, st, _ = blk.profile(to_dev(x))
+        assert st["gate_up"] > 0
+
+
+def test_decode_kernel_layer_step_vs_oracle():
+    """The decoder layer's FFN half at T=4 (RMSNorm, then the decode kernel with the
+    residual added in its combine) against the oracle layer."""
+    torch = _torch()
+    import oracle as O
+    from gpu_util import dev_bits, to_dev
+    cfg = S.QWEN15_MOE_A27B
+    bw, blk = _block(cfg, 0)
+    x = S.host_x(1600, 4, cfg.hidden)
+    nw = S.f32_to_bf16_bits(np.random.default_rng(4).uniform(0.5, 1.5, cfg.hidden).astype(np.float32))
+    out = blk.forward_layer(to_dev(x), to_dev(nw), 1e-6)
+    torch.cuda.synchronize()
+    y, _, _, _ = O.layer_ffn_forward(bw, x, nw, 1e-6)
+    assert_close(dev_bits(out).reshape(y.shape), y, "decode kernel layer step")

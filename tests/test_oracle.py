@@ -184,3 +184,15 @@ def test_layer_ffn_oracle_is_norm_block_residual():
     assert np.array_equal(out, S.f32_to_bf16_bits(S.bf16_bits_to_f32(x) + S.bf16_bits_to_f32(y)))
     two = O.residual_stack_forward([bw, bw], [nw, nw], x, 1e-6)
     assert np.array_equal(two, O.layer_ffn_forward(bw, out, nw, 1e-6)[0])
+
+
+def test_topk_nan_keys_rank_last_and_stay_distinct():
+    """A token with NaN scores (a non-finite activation) still selects k distinct, valid
+    experts: NaN keys rank after every other key, by index among themselves (the rule the
+    device top-k applies, so both pick the same set)."""
+    nan, one, two = 0x7FC0, 0x3F80, 0x4000
+    keys = np.array([[nan, one, nan, two, nan, nan],
+                     [nan] * 6,
+                     [two, nan, one, nan, nan, two]], np.uint16)
+    idx = O.topk_rows(keys, 4)
+    assert idx.tolist() == [[3, 1, 0, 2], [0, 1, 2, 3], [0, 5, 2, 1]]
