@@ -504,6 +504,9 @@ def block_roofline(cfg, regime, T, stage_ms, U, ms):
     if regime == "prefill":
         kind = "tcgen05 grouped GEMM" if P >= 32 * cfg.num_experts else "qgemv"
         return tensor_roofline(f"{kind} {dom}", flops[dom], stage_ms[dom], extra)
+    if stage_ms["down"] == 0.0 and stage_ms["router"] == 0.0:
+        # the one-launch decode kernel: its whole time is booked as the gate/up stage
+        return hbm_roofline("decode_block_kernel (whole block, one launch)", block_bytes, stage_ms["gate_up"], extra)
     return hbm_roofline(f"qgemv {dom}", alg[dom], stage_ms[dom], extra)
 
 

@@ -194,7 +194,9 @@ int moe_block_route(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_w
  * moe_block_forward with CUDA events between its stages; blocks until the block has
  * run. stage_ms[8] receives the device time of: router, top-k, grouping, gate/up,
  * down, shared gate/up, shared down, combine; n_active (optional) the number of
- * distinct experts the routing selected. Replaces the per-stage timers of
+ * distinct experts the routing selected. When the block ran as the one-launch decode
+ * kernel (the smallest batches), its whole time is the gate/up entry and the other seven
+ * are zero. Replaces the per-stage timers of
  * MoeProfileStats (qwen3_moe_python_port.rs:53-158, lfm2_moe_python_port.rs trace
  * stats), which time graph construction on the host rather than device work.
  */

@@ -24,6 +24,7 @@ struct moe_ctx {
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
   std::string last_error;
+  bool last_block_fused = false;  // the last block call ran the one-launch decode kernel
 };
 
 namespace {
@@ -133,6 +134,7 @@ struct BlockWs {
   float* tc_partial;    // split-K partials of the shared expert's tcgen05 GEMMs
   size_t tc_partial_bytes;
   uint16_t* xnorm;      // RMSNorm(x) of the decoder-layer step
+  uint16_t* logits_rep; // replicated router logits of the decode kernel (T <= kDecodeMaxT)
   size_t bytes;
 };
 
@@ -197,6 +199,7 @@ BlockWs carve_block(void* base, const moe_block_config* c, int64_t T) {
   w.tc_partial = ntc ? cv.take<float>(ntc) : nullptr;
   w.tc_partial_bytes = ntc * sizeof(float);
   w.xnorm = cv.take<uint16_t>(T * c->hidden);
+  if (T <= moe::kDecodeMaxT) w.logits_rep = cv.take<uint16_t>((size_t)moe::kDecodeLogitReplicas * T * (E + 1));
   w.bytes = cv.off + 256;
   return w;
 }
@@ -451,16 +454,22 @@ int run_route(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights* 
   return MOE_OK;
 }
 
-// Decode-sized batches (T <= 8 tokens, T * k <= 64 pairs) run the whole block in one
+// The smallest batches (T <= kDecodeFusedDefaultT tokens) run the whole block in one
 // cooperative kernel when the shapes fit its shared memory and every scale / bias array
-// is 4-byte aligned; MOE_B200_DECODE=0 in the environment keeps the launch chain.
+// is 4-byte aligned: measured on the B200 with the L2 flushed, a Qwen3-30B-A3B block at
+// T = 1 takes 34.8 us against 41.0 us for the launch chain (Qwen1.5-MoE 53 against 59 us),
+// while at T = 8 the chain is faster (72 against 103 us: the kernel's gate/up phase, one
+// 16-row unit per warp, streams at ~3 TB/s). MOE_B200_DECODE=1 takes the kernel for every
+// T <= kDecodeMaxT, =0 never.
+constexpr int kDecodeFusedDefaultT = 2;
 constexpr int kDecodeBarrierWord = 60;  // grid barrier word of the decode kernel, in the status block
 static_assert(kDecodeBarrierWord >= kFusedCounterWord + moe::kFusedRouteCounters && kDecodeBarrierWord < 64,
               "status block");
 bool decode_fused_ok(const moe_block_config* c, const moe_block_weights* w, int64_t T) {
   const char* v = std::getenv("MOE_B200_DECODE");
   if (v && v[0] == '0') return false;
-  if (T > moe::kDecodeMaxT || !moe::decode_smem_bytes((int)T, c->top_k, c->hidden, c->moe_inter, c->shared_inter))
+  if (!(v && v[0] == '1') && T > kDecodeFusedDefaultT) return false;
+  if (T > moe::kDecodeMaxT || !moe::decode_smem_bytes((int)T, c->top_k, c->num_experts, c->hidden, c->moe_inter, c->shared_inter))
     return false;
   const moe_qweight* m[6] = {&w->gate, &w->up, &w->down, &w->shared_gate, &w->shared_up, &w->shared_down};
   for (int i = 0; i < (c->shared_inter > 0 ? 6 : 3); ++i)
@@ -650,19 +659,23 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
       q(wts->shared_up, d.swu, d.ssu, d.sbu);
       q(wts->shared_down, d.swd, d.ssd, d.sbd);
     }
+    d.logits_rep = ws.logits_rep;
     d.hbuf = ws.hbuf;
     d.hsbuf = ws.hs;
     d.residual = static_cast<const uint16_t*>(residual);
     d.out = static_cast<uint16_t*>(out);
     d.barrier = reinterpret_cast<uint32_t*>(ws.status) + kDecodeBarrierWord;
     d.status = ws.status;
+    d.n_active = ws.n_active;
     d.has_gate = cfg->shared_inter > 0 && cfg->has_shared_gate;
     d.scale8 = decode_scale8(cfg, wts);
     for (int i = kRouter; i <= kGateUp; ++i) MOE_MARK(ev, i, ctx->stream);
     MOE_CUDA(ctx, moe::launch_decode_block(d, ctx->stream));
     for (int i = kDown; i <= kStages; ++i) MOE_MARK(ev, i, ctx->stream);
+    ctx->last_block_fused = true;
     return MOE_OK;
   }
+  ctx->last_block_fused = false;
   const ExpertPlan plan = plan_experts(P, E, I, H);
   rc = run_route(ctx, cfg, wts, x, T, ws, ev, nullptr, plan.min_rows);
   if (rc) return rc;
@@ -1027,7 +1040,13 @@ int moe_block_profile(moe_ctx* ctx, const moe_block_config* cfg, const moe_block
   int rc = run_block(ctx, cfg, wts, x, T, out, T > 0 ? ev : nullptr);
   if (rc == MOE_OK && T > 0) {
     cudaError_t e = cudaEventSynchronize(ev[kStages]);
-    for (int i = 0; i < kStages && e == cudaSuccess; ++i) e = cudaEventElapsedTime(&stage_ms[i], ev[i], ev[i + 1]);
+    if (ctx->last_block_fused) {
+      // one launch: its whole device time is the gate/up stage, the others are zero
+      for (int i = 0; i < kStages; ++i) stage_ms[i] = 0.0f;
+      e = cudaEventElapsedTime(&stage_ms[kGateUp], ev[kRouter], ev[kStages]);
+    } else {
+      for (int i = 0; i < kStages && e == cudaSuccess; ++i) e = cudaEventElapsedTime(&stage_ms[i], ev[i], ev[i + 1]);
+    }
     if (e != cudaSuccess) rc = fail(ctx, MOE_ERR_CUDA, "moe_block_profile: %s", cudaGetErrorString(e));
     if (rc == MOE_OK) {
       BlockWs ws = carve_block(ctx->scratch, cfg, T);

@@ -169,6 +169,7 @@ cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st);
 constexpr int kDecodeMaxT = 8;
 constexpr int kDecodeMaxP = 64;
 constexpr int kDecodeWarps = 8;
+constexpr int kDecodeLogitReplicas = 16;
 struct DecodeArgs {
   RouterArgs ra;             // logits into scratch [T, n_rows]
   TopkArgs ta;               // scoring / top-k / renorm options (output pointers unused)
@@ -179,17 +180,20 @@ struct DecodeArgs {
   const uint32_t* swg; const uint16_t* ssg; const uint16_t* sbg;  // shared gate [Is, H/8]
   const uint32_t* swu; const uint16_t* ssu; const uint16_t* sbu;  // shared up   [Is, H/8]
   const uint32_t* swd; const uint16_t* ssd; const uint16_t* sbd;  // shared down [H, Is/8]
+  uint16_t* logits_rep;      // [kDecodeLogitReplicas][T, n_rows] scratch: the router's logits,
+                             // replicated so that the CTAs' reads spread over many L2 lines
   uint16_t* hbuf;            // [T*k, I] scratch (pair order)
   uint16_t* hsbuf;           // [T, Is] scratch
   const uint16_t* residual;  // [T, H] added last, or null
   uint16_t* out;             // [T, H]
   uint32_t* barrier;         // grid barrier word (any value; left consistent after each call)
   int32_t* status;           // device status word (bounded waits)
+  int32_t* n_active;         // receives the number of distinct experts selected (or null)
   int has_gate;              // the shared expert is gated by sigmoid(logit row E)
   int scale8;                // 1: every scale/bias row pair of 4 groups is one 8-byte copy
 };
 // Dynamic shared memory of the decode kernel (0: the shapes do not fit it).
-size_t decode_smem_bytes(int T, int k, int H, int I, int Is);
+size_t decode_smem_bytes(int T, int k, int E, int H, int I, int Is);
 cudaError_t launch_decode_block(const DecodeArgs& a, cudaStream_t st);
 
 // One gather_qmm (out[i] = x[row(i)] . dequant(w[rhs[i]])^T, out in the caller's row

@@ -587,9 +587,10 @@ def test_decode_kernel_matches_launch_chain_and_oracle(cfg_name, seed, monkeypat
         assert st["gate_up"] > 0
 
 
-def test_decode_kernel_layer_step_vs_oracle():
+def test_decode_kernel_layer_step_vs_oracle(monkeypatch):
     """The decoder layer's FFN half at T=4 (RMSNorm, then the decode kernel with the
     residual added in its combine) against the oracle layer."""
+    monkeypatch.setenv("MOE_B200_DECODE", "1")
     torch = _torch()
     import oracle as O
     from gpu_util import dev_bits, to_dev
