@@ -177,6 +177,26 @@ int moe_layer_ffn_forward(moe_ctx* ctx, const moe_block_config* cfg, const moe_b
                           void* out);
 
 /*
+ * The Gemma4 MoE block: out[T, H] (f32) = SparseMoeBlock::forward of
+ * crates/mlx-models/src/gemma4.rs:1063-1085 with its Router (:906-936) and its GELU SwitchGlu
+ * (:1045-1052). The router normalises x (RMSNorm with a unit weight, eps 1e-6), multiplies
+ * by hidden^-0.5 and router_scale [H] (bf16) in f32, takes f32 logits through
+ * wts->router, selects the top_k experts by logit, and weights them by
+ * softmax(logits)[idx] / sum * per_expert_scale[idx] ([E] bf16), all in f32; the experts
+ * compute down(gelu_approx(gate(x)) * up(x)); the block output is the f32 weighted sum.
+ * cfg->scoring, norm_topk_prob and has_shared_gate are ignored; shared_inter must be 0.
+ * idx_out [T, k] and weights_out [T, k] (f32) optional. Differences from the reference,
+ * all inside the parity tolerance: the expert hidden h = gelu(gate) * up is rounded to
+ * bf16 before the down projection and the expert outputs are rounded to bf16 before the
+ * combine (the kernels' MMA operands and outputs are bf16; the reference keeps both f32).
+ * The reference's block is private; SparseMoeBlock::forward in gemma4.rs is what this
+ * replaces.
+ */
+int moe_gemma4_block_forward(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts,
+                             const void* router_scale, const void* per_expert_scale, const void* x, int64_t T,
+                             float* out, uint32_t* idx_out, float* weights_out);
+
+/*
  * Routing only (R1-R4 plus the per-expert grouping gather_qmm forms internally):
  *   idx[T, k] uint32      selected experts, by (score desc, index asc);
  *   weights[T, k] bf16    combine weights (renormalised when norm_topk_prob);

@@ -83,6 +83,9 @@ SIGNATURES = {
     "moe_layer_ffn_forward": (C.c_int, [C.c_void_p, C.POINTER(BlockConfig), C.POINTER(BlockWeights),
                                         C.c_void_p, C.c_int64, C.c_void_p, C.c_float, C.c_void_p,
                                         C.c_void_p]),
+    "moe_gemma4_block_forward": (C.c_int, [C.c_void_p, C.POINTER(BlockConfig), C.POINTER(BlockWeights),
+                                           C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p,
+                                           C.c_void_p, C.c_void_p]),
     "moe_block_profile": (C.c_int, [C.c_void_p, C.POINTER(BlockConfig), C.POINTER(BlockWeights),
                                     C.c_void_p, C.c_int64, C.c_void_p, C.POINTER(C.c_float),
                                     C.POINTER(C.c_int32)]),

@@ -158,6 +158,40 @@ class MoeFeedForward(_Block):
         super().__init__(weights, cfg)
 
 
+class Gemma4MoeBlock(_Block):
+    """Gemma4 SparseMoeBlock (crates/mlx-models/src/gemma4.rs:1054-1085): Router::forward
+    (:906-936: RMSNorm(x) * hidden^-0.5 * scale in f32, top-k by logit, weights
+    softmax[idx] / sum * per_expert_scale[idx]) and the GELU SwitchGlu (:1045-1052). The
+    block's output is f32, as in the reference (its router and GELU constants are 0-d f32
+    arrays). One call of moe_gemma4_block_forward."""
+
+    def __init__(self, weights: BlockWeights, router_scale: torch.Tensor, per_expert_scale: torch.Tensor):
+        super().__init__(weights)
+        if router_scale.dtype != torch.bfloat16 or per_expert_scale.dtype != torch.bfloat16:
+            raise MlxError("moe_gemma4_block_forward", 1, "scale and per_expert_scale must be bf16")
+        self.router_scale = router_scale.contiguous()
+        self.per_expert_scale = per_expert_scale.contiguous()
+
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None, routing: bool = False):
+        H, k = self.config.hidden, self.config.top_k
+        fn = "moe_gemma4_block_forward"
+        if x.shape[-1] != H or x.dtype != torch.bfloat16 or not x.is_contiguous():
+            raise MlxError(fn, 1, "x must be contiguous bf16 [..., hidden]")
+        T = x.numel() // H
+        if out is None:
+            out = torch.empty(*x.shape, dtype=torch.float32, device=x.device)
+        idx = torch.empty(T, k, dtype=torch.int32, device=x.device) if routing else None
+        w = torch.empty(T, k, dtype=torch.float32, device=x.device) if routing else None
+        ctx = _ctx(x)
+        rc = library().moe_gemma4_block_forward(ctx.handle, C.byref(self._cfg), C.byref(self._wts),
+                                                _ptr(self.router_scale), _ptr(self.per_expert_scale), _ptr(x), T,
+                                                _ptr(out), _ptr(idx), _ptr(w))
+        ctx.check(fn, rc)
+        return (out, idx, w) if routing else out
+
+    __call__ = forward
+
+
 class RmsNorm:
     def __init__(self, weight: torch.Tensor, eps: float = 1e-6):
         self.weight, self.eps = weight, eps
@@ -193,5 +227,5 @@ class MoeStack:
     __call__ = forward
 
 
-__all__ = ["SwitchLinear", "SparseMoeBlock", "MoeFeedForward", "RmsNorm", "MoeStack", "infer_bits",
+__all__ = ["SwitchLinear", "SparseMoeBlock", "MoeFeedForward", "Gemma4MoeBlock", "RmsNorm", "MoeStack", "infer_bits",
            "SCORING_SOFTMAX", "SCORING_SOFTMAX_BIAS", "SCORING_SIGMOID_BIAS_SELECT"]

@@ -11,6 +11,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <cmath>
 #include <cstring>
 #include <new>
 #include <string>
@@ -618,6 +619,71 @@ moe::QgemvArgs qgemv_args(const moe_qweight& m0, const moe_qweight* m1, int N, i
 
 namespace {
 
+// The routed experts of a block call after its routing and grouping: SwitchGLU gate/up
+// (SiLU * up, act 0; GELU-tanh * up, act 1) and down over the grouped pairs, each expert
+// on the GEMV or the tcgen05 GEMM as plan says; expert outputs into ws.ybuf.
+int run_routed_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x,
+                       int64_t T, const BlockWs& ws, const ExpertPlan& plan, cudaEvent_t* ev, int act) {
+  const int E = cfg->num_experts, H = cfg->hidden, I = cfg->moe_inter, k = cfg->top_k;
+  const int64_t P = T * k;
+  const int slots = (int)std::min<int64_t>(P, E);
+  // Expected rows per expert: how many tokens one GEMV pass over the weights serves.
+  const int rows_pe = (int)std::min<int64_t>((P + E - 1) / E, 1 << 20);
+  // SwitchGLU gate/up + SiLU*up over grouped rows (x row = pair / k).
+  moe::QgemvArgs gu = qgemv_args(wts->gate, &wts->up, I, H);
+  gu.x = static_cast<const uint16_t*>(x);
+  gu.x_mode = 1;
+  gu.x_repeat = k;
+  gu.perm = ws.perm;
+  gu.offsets = ws.offsets;
+  gu.active = ws.active;
+  gu.n_active = ws.n_active;
+  gu.out = ws.hbuf;
+  gu.out_mode = 0;
+  gu.partial = ws.gemv_partial;
+  gu.partial_bytes = ws.gemv_partial_bytes;
+  gu.part_rows = P;
+  gu.num_experts_total = E;
+  gu.act = act;
+  MOE_MARK(ev, kGateUp, ctx->stream);
+  // GEMV first: at decode sizes it carries the work, and the (mostly idle) tcgen05
+  // launch behind it overlaps its tail under programmatic dependent launch.
+  if (plan.gemv_gu) {
+    gu.max_expert_rows = plan.gemv_skip_gu;
+    MOE_CUDA(ctx, moe::launch_qgemv(gu, true, slots, rows_pe, ctx->stream));
+  }
+  if (plan.tc_gu) {
+    moe::TcGemmArgs ta{gu, ws.tile_start, E, plan.max_tiles, ws.status};
+    MOE_CUDA(ctx, moe::launch_tc_gemm(ta, true, ctx->stream));
+  }
+
+  // down projection over the same grouped rows.
+  moe::QgemvArgs dn = qgemv_args(wts->down, nullptr, H, I);
+  dn.x = ws.hbuf;
+  dn.x_mode = 0;
+  dn.perm = ws.perm;
+  dn.offsets = ws.offsets;
+  dn.active = ws.active;
+  dn.n_active = ws.n_active;
+  dn.out = ws.ybuf;
+  dn.out_mode = 0;
+  dn.partial = ws.gemv_partial;
+  dn.partial_bytes = ws.gemv_partial_bytes;
+  dn.part_rows = P;
+  dn.num_experts_total = E;
+  MOE_MARK(ev, kDown, ctx->stream);
+  if (plan.gemv_dn) {
+    dn.max_expert_rows = plan.gemv_skip_dn;
+    MOE_CUDA(ctx, moe::launch_qgemv(dn, false, slots, rows_pe, ctx->stream));
+  }
+  if (plan.tc_dn) {
+    moe::TcGemmArgs ta{dn, ws.tile_start, E, plan.max_tiles, ws.status};
+    MOE_CUDA(ctx, moe::launch_tc_gemm(ta, false, ctx->stream));
+  }
+
+  return MOE_OK;
+}
+
 int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x, int64_t T,
               void* out, cudaEvent_t* ev, const void* residual = nullptr) {
   if (!ctx) return MOE_ERR_INVALID;
@@ -680,59 +746,8 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
   rc = run_route(ctx, cfg, wts, x, T, ws, ev, nullptr, plan.min_rows);
   if (rc) return rc;
 
-  const int slots = (int)std::min<int64_t>(P, E);
-  // Expected rows per expert: how many tokens one GEMV pass over the weights serves.
-  const int rows_pe = (int)std::min<int64_t>((P + E - 1) / E, 1 << 20);
-  // SwitchGLU gate/up + SiLU*up over grouped rows (x row = pair / k).
-  moe::QgemvArgs gu = qgemv_args(wts->gate, &wts->up, I, H);
-  gu.x = static_cast<const uint16_t*>(x);
-  gu.x_mode = 1;
-  gu.x_repeat = k;
-  gu.perm = ws.perm;
-  gu.offsets = ws.offsets;
-  gu.active = ws.active;
-  gu.n_active = ws.n_active;
-  gu.out = ws.hbuf;
-  gu.out_mode = 0;
-  gu.partial = ws.gemv_partial;
-  gu.partial_bytes = ws.gemv_partial_bytes;
-  gu.part_rows = P;
-  gu.num_experts_total = E;
-  MOE_MARK(ev, kGateUp, ctx->stream);
-  // GEMV first: at decode sizes it carries the work, and the (mostly idle) tcgen05
-  // launch behind it overlaps its tail under programmatic dependent launch.
-  if (plan.gemv_gu) {
-    gu.max_expert_rows = plan.gemv_skip_gu;
-    MOE_CUDA(ctx, moe::launch_qgemv(gu, true, slots, rows_pe, ctx->stream));
-  }
-  if (plan.tc_gu) {
-    moe::TcGemmArgs ta{gu, ws.tile_start, E, plan.max_tiles, ws.status};
-    MOE_CUDA(ctx, moe::launch_tc_gemm(ta, true, ctx->stream));
-  }
-
-  // down projection over the same grouped rows.
-  moe::QgemvArgs dn = qgemv_args(wts->down, nullptr, H, I);
-  dn.x = ws.hbuf;
-  dn.x_mode = 0;
-  dn.perm = ws.perm;
-  dn.offsets = ws.offsets;
-  dn.active = ws.active;
-  dn.n_active = ws.n_active;
-  dn.out = ws.ybuf;
-  dn.out_mode = 0;
-  dn.partial = ws.gemv_partial;
-  dn.partial_bytes = ws.gemv_partial_bytes;
-  dn.part_rows = P;
-  dn.num_experts_total = E;
-  MOE_MARK(ev, kDown, ctx->stream);
-  if (plan.gemv_dn) {
-    dn.max_expert_rows = plan.gemv_skip_dn;
-    MOE_CUDA(ctx, moe::launch_qgemv(dn, false, slots, rows_pe, ctx->stream));
-  }
-  if (plan.tc_dn) {
-    moe::TcGemmArgs ta{dn, ws.tile_start, E, plan.max_tiles, ws.status};
-    MOE_CUDA(ctx, moe::launch_tc_gemm(ta, false, ctx->stream));
-  }
+  rc = run_routed_experts(ctx, cfg, wts, x, T, ws, plan, ev, 0);
+  if (rc) return rc;
 
   const bool shared = cfg->shared_inter > 0;
   if (!shared) {
@@ -994,6 +1009,99 @@ int moe_block_route(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_w
 int moe_block_forward(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x,
                       int64_t T, void* out) {
   return run_block(ctx, cfg, wts, x, T, out, nullptr);
+}
+
+int moe_gemma4_block_forward(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts,
+                             const void* router_scale, const void* per_expert_scale, const void* x, int64_t T,
+                             float* out, uint32_t* idx_out, float* weights_out) {
+  if (!ctx) return MOE_ERR_INVALID;
+  ctx->last_error.clear();
+  const char* fn = "moe_gemma4_block_forward";
+  if (!cfg) return fail(ctx, MOE_ERR_INVALID, "%s: null config", fn);
+  moe_block_config c = *cfg;  // scoring, renormalisation and gate are fixed by the variant
+  c.scoring = MOE_SCORING_SOFTMAX;
+  c.norm_topk_prob = 1;
+  c.has_shared_gate = 0;
+  if (c.shared_inter != 0)
+    return fail(ctx, MOE_ERR_UNSUPPORTED, "%s: the Gemma4 block has no shared expert (shared_inter=%d)", fn,
+                c.shared_inter);
+  int rc = check_block(ctx, &c, wts, fn);
+  if (rc) return rc;
+  if (T < 0 || T > (INT32_MAX / 64)) return fail(ctx, MOE_ERR_INVALID, "%s: bad T", fn);
+  if (T == 0) return MOE_OK;
+  if (!x || !out || !router_scale || !per_expert_scale || !aligned16(x) || !aligned16(out) ||
+      !aligned16(router_scale))
+    return fail(ctx, MOE_ERR_INVALID, "%s: x, out, router_scale (16-byte aligned) and per_expert_scale required",
+                fn);
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  const int E = c.num_experts, H = c.hidden, k = c.top_k;
+  // the block workspace, then the router's f32 input rows, f32 logits and f32 weights
+  auto carve = [&](void* base, BlockWs& ws, float*& hf, float*& lf, float*& wf) {
+    ws = carve_block(base, &c, T);
+    Carve cv(base);
+    cv.off = ws.bytes;
+    hf = cv.take<float>((size_t)T * H);
+    lf = cv.take<float>((size_t)T * E);
+    wf = cv.take<float>((size_t)T * k);
+    return cv.off + 256;
+  };
+  BlockWs ws;
+  float *hf, *lf, *wf;
+  rc = ensure_scratch(ctx, carve(nullptr, ws, hf, lf, wf));
+  if (rc) return rc;
+  carve(ctx->scratch, ws, hf, lf, wf);
+  const int64_t P = T * k;
+  // router input: RMSNorm(x) (unit weight, eps 1e-6) * hidden^-0.5 * scale, in f32
+  const float root = (float)(1.0 / std::sqrt((double)H));
+  MOE_CUDA(ctx, moe::launch_gemma_router_input(static_cast<const uint16_t*>(x),
+                                               static_cast<const uint16_t*>(router_scale), root, 1e-6f, T, H, hf,
+                                               ctx->stream));
+  moe::RouterArgs ra{};
+  moe::TopkArgs ta{};
+  route_args(&c, wts, x, T, ws, ra, ta);
+  ra.xf = hf;
+  ra.logits_f32 = lf;
+  MOE_CUDA(ctx, moe::launch_router(ra, ctx->stream));
+  ta.scoring = 3;
+  ta.logits_f32 = lf;
+  ta.per_expert_scale = static_cast<const uint16_t*>(per_expert_scale);
+  ta.weights_f32 = wf;
+  ta.idx = ws.idx;
+  ta.weights = nullptr;
+  MOE_CUDA(ctx, moe::launch_topk(ta, ctx->stream));
+  const ExpertPlan plan = plan_experts(P, E, c.moe_inter, H);
+  moe::GroupArgs ga{};
+  ga.key = ws.idx;
+  ga.P = P;
+  ga.E = E;
+  ga.seg = moe::group_seg(P, E);
+  ga.nseg = (int)std::max<int64_t>(1, (P + ga.seg - 1) / ga.seg);
+  ga.hist = ws.hist;
+  ga.segbase = ws.segbase;
+  ga.offsets = ws.offsets;
+  ga.active = ws.active;
+  ga.n_active = ws.n_active;
+  ga.perm = ws.perm;
+  ga.inv = ws.inv;
+  ga.tile_start = ws.tile_start;
+  ga.tile_rows = moe::kTcTileRows;
+  ga.tc_min_rows = plan.min_rows;
+  MOE_CUDA(ctx, moe::launch_group(ga, ctx->stream));
+  rc = run_routed_experts(ctx, &c, wts, x, T, ws, plan, nullptr, 1);
+  if (rc) return rc;
+  moe::CombineArgs ca{};
+  ca.y = ws.ybuf;
+  ca.inv = ws.inv;
+  ca.weights_f32 = wf;
+  ca.out_f32 = out;
+  ca.T = (int)T;
+  ca.k = k;
+  ca.H = H;
+  MOE_CUDA(ctx, moe::launch_combine(ca, ctx->stream));
+  if (idx_out) MOE_CUDA(ctx, cudaMemcpyAsync(idx_out, ws.idx, P * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  if (weights_out) MOE_CUDA(ctx, cudaMemcpyAsync(weights_out, wf, P * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  return MOE_OK;
 }
 
 int moe_layer_ffn_forward(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts,

@@ -127,10 +127,93 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const uint16_t* __restric
   }
 }
 
+// The Gemma4 block's combine (gemma4.rs:1079-1083): out[t] (f32) = sum over j in order of
+// f32(y[t, j]) * w[t, j], the weights and the sum in f32 (its expert outputs and weights
+// are f32 in the reference; y here is the bf16 output of the down projection).
+__global__ void __launch_bounds__(256) combine_f32_kernel(CombineArgs a) {
+  const int vec_per_row = a.H >> 3;
+  const int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  if (id >= (int64_t)a.T * vec_per_row) return;
+  const int t = (int)(id / vec_per_row);
+  const int h = (int)(id - (int64_t)t * vec_per_row) * 8;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+  for (int j = 0; j < a.k; ++j) {
+    const int64_t p = (int64_t)t * a.k + j;
+    const float w = a.weights_f32[p];
+    const uint4 v = *reinterpret_cast<const uint4*>(a.y + (size_t)a.inv[p] * a.H + h);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      acc[2 * i] = __fadd_rn(acc[2 * i], __fmul_rn(bf_lo(u[i]), w));
+      acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __fmul_rn(bf_hi(u[i]), w));
+    }
+  }
+  float4* o = reinterpret_cast<float4*>(a.out_f32 + (size_t)t * a.H + h);
+  o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+}
+
+// out[r] = f32(bf16(x[r] * rsqrt(mean(x[r]^2) + eps))) * root * f32(scale): the Gemma4
+// router's input (gemma4.rs:911-919: fast_rms_norm with a ones weight, then two multiplies
+// by 0-d f32 arrays, which makes the rest of the router f32). The norm as rms_norm_kernel.
+__global__ void __launch_bounds__(256) gemma_router_input_kernel(const uint16_t* __restrict__ x,
+                                                                 const uint16_t* __restrict__ scale, float root,
+                                                                 float eps, int64_t rows, int dim,
+                                                                 float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  pdl_wait();
+  pdl_trigger();
+  if (r >= rows) return;
+  const uint16_t* xr = x + (size_t)r * dim;
+  const int nchunks = dim >> 3;
+  float acc = 0.0f;
+  for (int c = lane; c < nchunks; c += 32) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + c * 8);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float lo = bf_lo(u[i]), hi = bf_hi(u[i]);
+      acc = __fmaf_rn(lo, lo, acc);
+      acc = __fmaf_rn(hi, hi, acc);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+  const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)dim), eps)));
+  for (int c = lane; c < nchunks; c += 32) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + c * 8);
+    const uint4 sv = *reinterpret_cast<const uint4*>(scale + c * 8);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    const uint32_t su[4] = {sv.x, sv.y, sv.z, sv.w};
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      o[2 * i] = __fmul_rn(__fmul_rn(rbf(__fmul_rn(bf_lo(u[i]), rr)), root), bf_lo(su[i]));
+      o[2 * i + 1] = __fmul_rn(__fmul_rn(rbf(__fmul_rn(bf_hi(u[i]), rr)), root), bf_hi(su[i]));
+    }
+    float4* op = reinterpret_cast<float4*>(out + (size_t)r * dim + c * 8);
+    op[0] = make_float4(o[0], o[1], o[2], o[3]);
+    op[1] = make_float4(o[4], o[5], o[6], o[7]);
+  }
+}
+
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st) {
   const int64_t n = (int64_t)a.T * (a.H >> 3);
   if (n <= 0) return cudaSuccess;
+  if (a.weights_f32) return launch_k(combine_f32_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, a);
   return launch_k(combine_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, a);
+}
+
+cudaError_t launch_gemma_router_input(const uint16_t* x, const uint16_t* scale, float root, float eps, int64_t rows,
+                                      int dim, float* out, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  return launch_k(gemma_router_input_kernel, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0, st, x, scale, root, eps,
+                  rows, dim, out);
 }
 
 cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, float eps, int64_t rows, int dim,

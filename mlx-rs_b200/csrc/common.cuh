@@ -66,6 +66,19 @@ MOE_DEV uint16_t swiglu_bf16(float g, float u) {
   return f2bf(__fmul_rn(a, u));
 }
 
+// h = bf16(gelu_approx(g) * u) for the Gemma4 SwitchGLU (gemma4.rs:308-322, 1049): the
+// reference evaluates in f32 (its constants are 0-d f32 arrays):
+//   0.5 * (g * (1 + tanh(sqrt(2/pi) * (g + 0.044715 * g^3)))) * u,
+// with g^3 as two multiplies (the reference's power(x, 3)) and CUDA's tanhf; the product is
+// rounded to bf16, the operand type of the down projection's MMA (the reference keeps f32).
+MOE_DEV uint16_t gelu_mul_bf16(float g, float u) {
+  const float x3 = __fmul_rn(__fmul_rn(g, g), g);
+  const float inner = __fmul_rn(__fadd_rn(g, __fmul_rn(x3, 0x1.6e4e26p-5f)), 0x1.988452p-1f);
+  const float gate = __fadd_rn(1.0f, tanhf(inner));
+  const float h = __fmul_rn(0.5f, __fmul_rn(g, gate));
+  return f2bf(__fmul_rn(h, u));
+}
+
 // Programmatic dependent launch: kernels of the block are launched so that each may
 // start while its predecessor in the stream drains. pdl_wait() blocks until the
 // predecessor grid has completed and its writes are visible (a no-op when the kernel

@@ -41,6 +41,8 @@ struct RouterArgs {
   const uint16_t* gate_s;
   const uint16_t* gate_b;
   uint16_t* logits;
+  const float* xf;     // f32 token rows (stride K) in place of x (the Gemma4 router), or null
+  float* logits_f32;   // f32 logits [T, n_rows], not rounded (with xf), or null
 };
 
 struct TopkArgs {
@@ -51,6 +53,11 @@ struct TopkArgs {
   uint16_t* weights;            // [T, k] bf16
   uint16_t* gate_val;           // [T] bf16 = sigmoid(logits[:, E]) or null
   uint32_t* packed;             // [T, k] idx | bf16(weight) << 16, or null
+  // scoring 3 (the Gemma4 router): f32 logits in, top-k by logit, f32 weights
+  // softmax(logits)[idx] / sum * per_expert_scale[idx] out
+  const float* logits_f32;      // [T, n_rows]
+  const uint16_t* per_expert_scale;  // [E] bf16
+  float* weights_f32;           // [T, k]
 };
 
 // Stable grouping of P pair ids by expert id. The expert of pair p is
@@ -105,12 +112,15 @@ struct QgemvArgs {
   size_t partial_bytes;
   int64_t part_rows;        // rows of the partial buffer (grouped positions; P or T)
   int num_experts_total;    // entries of offsets minus one (for the reduction's row check)
+  int act;                  // gated form: 0 SiLU(gate) * up in bf16 ops, 1 GELU-tanh(gate) * up in f32
 };
 
 struct CombineArgs {
   const uint16_t* y;        // [P, H] expert outputs in grouped order
   const uint32_t* inv;      // [P] pair -> grouped row
   const uint16_t* weights;  // [T, k] bf16
+  const float* weights_f32; // [T, k] f32 weights, f32 products and sum, f32 out_f32 (the Gemma4 block)
+  float* out_f32;           // [T, H]
   const uint16_t* shared;   // [T, H] shared expert output or null
   const uint16_t* gate_val; // [T] bf16 shared gate or null
   const uint16_t* residual; // [T, H] added last (the decoder layer's residual) or null
@@ -236,5 +246,9 @@ cudaError_t launch_ep_finish(const float* recv, int world, int64_t rows, int H, 
                              const uint16_t* norm_w, float eps, uint16_t* normed, cudaStream_t st);
 cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, float eps, int64_t rows, int dim,
                             uint16_t* out, cudaStream_t st);
+// The Gemma4 router's input: out[r] (f32) = f32(RMSNorm(x[r]) with unit weight, rounded to
+// bf16) * root * f32(scale), as launch_rms_norm computes the norm.
+cudaError_t launch_gemma_router_input(const uint16_t* x, const uint16_t* scale, float root, float eps, int64_t rows,
+                                      int dim, float* out, cudaStream_t st);
 
 }  // namespace moe

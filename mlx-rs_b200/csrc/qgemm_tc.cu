@@ -474,12 +474,19 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
         if (GATED) {
           uint32_t u[32];
           tmem_ld32(tl + 256 + c0, u);
+          if (a.act) {  // GELU-tanh(gate) * up in f32 (the Gemma4 SwitchGLU)
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            const uint32_t h2 = swiglu2_fast(__uint_as_float(g[j]), __uint_as_float(g[j + 1]),
-                                             __uint_as_float(u[j]), __uint_as_float(u[j + 1]));
-            *reinterpret_cast<uint16_t*>(tile + j * 64 + lane * 2) = (uint16_t)(h2 & 0xffffu);
-            *reinterpret_cast<uint16_t*>(tile + (j + 1) * 64 + lane * 2) = (uint16_t)(h2 >> 16);
+            for (int j = 0; j < 32; ++j)
+              *reinterpret_cast<uint16_t*>(tile + j * 64 + lane * 2) =
+                  gelu_mul_bf16(rbf(__uint_as_float(g[j])), rbf(__uint_as_float(u[j])));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              const uint32_t h2 = swiglu2_fast(__uint_as_float(g[j]), __uint_as_float(g[j + 1]),
+                                               __uint_as_float(u[j]), __uint_as_float(u[j + 1]));
+              *reinterpret_cast<uint16_t*>(tile + j * 64 + lane * 2) = (uint16_t)(h2 & 0xffffu);
+              *reinterpret_cast<uint16_t*>(tile + (j + 1) * 64 + lane * 2) = (uint16_t)(h2 >> 16);
+            }
           }
         } else {
 #pragma unroll

@@ -538,7 +538,9 @@ __global__ void __launch_bounds__(FK ? 512 : 256) qgemv_kernel(QgemvArgs a, int 
             for (int t = 0; t < MT; ++t) {
               if (GATED) {
                 const int row = r0 + 8 * t + gq;
-                if (row < N) o[row] = swiglu_bf16(rbf(acc[n][t][cc]), rbf(acc[n][t][2 + cc]));
+                if (row < N)
+                  o[row] = a.act ? gelu_mul_bf16(rbf(acc[n][t][cc]), rbf(acc[n][t][2 + cc]))
+                                 : swiglu_bf16(rbf(acc[n][t][cc]), rbf(acc[n][t][2 + cc]));
               } else {
                 const int row = r0 + 16 * t + gq;
                 if (row < N) o[row] = f2bf(acc[n][t][cc]);
@@ -815,7 +817,9 @@ __global__ void __launch_bounds__(512) qgemv_i8_kernel(QgemvArgs a, int units_pe
       for (int t = 0; t < MT; ++t) {
         if (GATED) {
           const int row = r0 + 8 * t + gq;
-          if (row < N) o[row] = swiglu_bf16(rbf(acc[t][0] * us), rbf(acc[t][1] * us));
+          if (row < N)
+            o[row] = a.act ? gelu_mul_bf16(rbf(acc[t][0] * us), rbf(acc[t][1] * us))
+                           : swiglu_bf16(rbf(acc[t][0] * us), rbf(acc[t][1] * us));
         } else {
           const int row = r0 + 16 * t + gq;
           if (row < N) o[row] = f2bf(acc[t][0] * us);
@@ -861,7 +865,8 @@ __global__ void __launch_bounds__(256) qgemv_reduce_kernel(QgemvArgs a, int num_
   }
   RowMap rm{a.x_mode, a.x_repeat, a.lhs, a.perm};
   const int64_t orow = a.out_mode == 0 ? pos : rm.orig(pos);
-  a.out[(size_t)orow * N + n] = GATED ? swiglu_bf16(rbf(g), rbf(u)) : f2bf(g);
+  a.out[(size_t)orow * N + n] =
+      GATED ? (a.act ? gelu_mul_bf16(rbf(g), rbf(u)) : swiglu_bf16(rbf(g), rbf(u))) : f2bf(g);
 }
 
 template <int MT, int NC, int NS, bool FK>

@@ -137,6 +137,88 @@ MOE_DEV void router_tile(const RouterArgs& a, int row0, int t0, int lane) {
   }
 }
 
+// router_tile for f32 token rows (a.xf) and unrounded f32 logits (a.logits_f32): the
+// Gemma4 router, whose input is RMSNorm(x) * root_size * scale in f32
+// (gemma4.rs:906-920). Same canonical order as router_tile.
+template <int NE, int NT>
+MOE_DEV void router_tile_f32(const RouterArgs& a, int row0, int t0, int lane) {
+  if (row0 >= a.n_rows) return;
+  const int nchunks = a.K >> 5;
+  const int wpr = a.K >> 3;
+  const int gpr = a.K / a.group_size;
+  float acc[NE][NT];
+#pragma unroll
+  for (int e = 0; e < NE; ++e)
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[e][t] = 0.0f;
+  const uint32_t* wrow[NE];
+  const uint16_t* srow[NE];
+  const uint16_t* brow[NE];
+  bool rvalid[NE];
+#pragma unroll
+  for (int e = 0; e < NE; ++e) {
+    const int r = row0 + e;
+    rvalid[e] = r < a.n_rows;
+    const int rr = r < a.n_rows ? r : 0;
+    wrow[e] = a.w + (size_t)rr * wpr;
+    srow[e] = a.s + (size_t)rr * gpr;
+    brow[e] = a.b ? a.b + (size_t)rr * gpr : nullptr;
+  }
+  for (int c = lane; c < nchunks; c += 32) {
+    const int g = (c * 32) / a.group_size;
+    float sc[NE], bi[NE];
+#pragma unroll
+    for (int e = 0; e < NE; ++e) {
+      sc[e] = rvalid[e] ? bf2f(__ldg(srow[e] + g)) : 0.0f;
+      bi[e] = (rvalid[e] && brow[e]) ? bf2f(__ldg(brow[e] + g)) : 0.0f;
+    }
+#pragma unroll 1
+    for (int word = 0; word < 4; ++word) {
+      uint32_t wv[NE];
+#pragma unroll
+      for (int e = 0; e < NE; ++e) wv[e] = rvalid[e] ? __ldg(wrow[e] + (size_t)c * 4 + word) : 0u;
+      float4 xl[NT], xh[NT];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        const int tok = t0 + t;
+        if (tok < a.T) {
+          const float4* p = reinterpret_cast<const float4*>(a.xf + (size_t)tok * a.K + c * 32 + word * 8);
+          xl[t] = __ldg(p);
+          xh[t] = __ldg(p + 1);
+        } else {
+          xl[t] = xh[t] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+      }
+#pragma unroll
+      for (int el = 0; el < 8; ++el) {
+        float wq[NE];
+#pragma unroll
+        for (int e = 0; e < NE; ++e) {
+          const float q = __fsub_rn(__uint_as_float(((wv[e] >> (4 * el)) & 0xfu) | 0x4b000000u), 8388608.0f);
+          wq[e] = __fmaf_rn(sc[e], q, bi[e]);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const float4 v = el < 4 ? xl[t] : xh[t];
+          const int j = el & 3;
+          const float xe = j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
+#pragma unroll
+          for (int e = 0; e < NE; ++e) acc[e][t] = __fmaf_rn(xe, wq[e], acc[e][t]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < NE; ++e)
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      float v = acc[e][t];
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+      if (lane == 0 && rvalid[e] && t0 + t < a.T) a.logits_f32[(size_t)(t0 + t) * a.n_rows + row0 + e] = v;
+    }
+}
+
 // (key desc, index asc), with NaN keys after every other key (NaN among NaN by index
 // asc): true if (ka, ia) ranks before (kb, ib). A strict total order, so every round of
 // the warp arg-max has one winner and the k selected experts are distinct and valid even
@@ -156,6 +238,7 @@ MOE_DEV bool ranks_before(float ka, int ia, float kb, int ib) {
 template <int PL>
 MOE_DEV void topk_token(const TopkArgs& a, int t, int lane) {
   const uint16_t* lrow = a.logits + (size_t)t * a.n_rows;
+  const bool gemma = a.scoring == 3;  // f32 logits, top-k by logit, f32 weights (no bf16 rounding)
 
   float val[PL], key[PL];
   float l[PL];
@@ -165,7 +248,7 @@ MOE_DEV void topk_token(const TopkArgs& a, int t, int lane) {
     const int e = lane + 32 * i;
     l[i] = 0.0f;
     if (e < a.E) {
-      float v = bf2f(__ldcg(lrow + e));
+      float v = gemma ? __ldcg(a.logits_f32 + (size_t)t * a.n_rows + e) : bf2f(__ldcg(lrow + e));
       if (a.scoring == 1) v = rbf(__fadd_rn(v, bf2f(a.expert_bias[e])));
       l[i] = v;
       m = fmaxf(m, v);
@@ -200,8 +283,8 @@ MOE_DEV void topk_token(const TopkArgs& a, int t, int lane) {
     for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
 #pragma unroll
     for (int i = 0; i < PL; ++i) {
-      val[i] = rbf(__fdiv_rn(ex[i], s));
-      key[i] = val[i];
+      val[i] = gemma ? __fdiv_rn(ex[i], s) : rbf(__fdiv_rn(ex[i], s));
+      key[i] = gemma ? l[i] : val[i];
     }
   }
 
@@ -244,6 +327,17 @@ MOE_DEV void topk_token(const TopkArgs& a, int t, int lane) {
       my_sel = bi;
       my_w = wv;
     }
+  }
+  if (gemma) {
+    // w = p / sum_j p_j (f32, j in order) * per_expert_scale (gemma4.rs:927-933)
+    float d = 0.0f;
+    for (int j = 0; j < a.k; ++j) d = __fadd_rn(d, __shfl_sync(0xffffffffu, my_w, j));
+    if (lane < a.k) {
+      const float w = __fmul_rn(__fdiv_rn(my_w, d), bf2f(a.per_expert_scale[my_sel]));
+      a.weights_f32[(size_t)t * a.k + lane] = w;
+      if (a.idx) a.idx[(size_t)t * a.k + lane] = (uint32_t)my_sel;
+    }
+    return;
   }
   if (a.norm_topk_prob) {
     float d = 0.0f;

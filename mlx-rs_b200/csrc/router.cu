@@ -26,6 +26,14 @@ __global__ void __launch_bounds__(128, 4) router_logits_kernel(RouterArgs a) {
   router_tile<NE, NT>(a, (blockIdx.x * 4 + warp) * NE, blockIdx.y * NT, lane);
 }
 
+template <int NE, int NT>
+__global__ void __launch_bounds__(128, 4) router_logits_f32_kernel(RouterArgs a) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  pdl_wait();
+  pdl_trigger();
+  router_tile_f32<NE, NT>(a, (blockIdx.x * 4 + warp) * NE, blockIdx.y * NT, lane);
+}
+
 template <int PL>
 __global__ void __launch_bounds__(128) topk_kernel(TopkArgs a) {
   const int lane = threadIdx.x & 31;
@@ -202,6 +210,10 @@ cudaError_t launch_route_fused(const RouterArgs& ra, const TopkArgs& ta, const G
 
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t st) {
   if (a.T <= 0) return cudaSuccess;
+  if (a.xf) {  // f32 token rows, f32 logits
+    if (a.T <= 4) return launch_k(router_logits_f32_kernel<1, 1>, dim3((a.n_rows + 3) / 4, a.T), dim3(128), 0, st, a);
+    return launch_k(router_logits_f32_kernel<2, 4>, dim3((a.n_rows + 7) / 8, (a.T + 3) / 4), dim3(128), 0, st, a);
+  }
   if (a.T <= 4) {
     dim3 grid((a.n_rows + 3) / 4, a.T);
     return launch_k(router_logits_kernel<1, 1>, grid, dim3(128), 0, st, a);

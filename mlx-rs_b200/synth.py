@@ -45,6 +45,10 @@ QWEN15_MOE_A27B = MoeConfig(2048, 60, 4, 1408, 5632, SCORING_SOFTMAX, False, Tru
 QWEN3_30B_A3B = MoeConfig(2048, 128, 8, 768, 0, SCORING_SOFTMAX, True, False, name="qwen3-30b-a3b")
 LFM2_8B_A1B = MoeConfig(2048, 32, 4, 1792, 0, SCORING_SIGMOID_BIAS_SELECT, True, False,
                         name="lfm2-8b-a1b")
+# A Gemma4-style block (gemma4.rs Router + GELU SwitchGlu). The reference names no Gemma4
+# MoE configuration, so this shape is synthetic: hidden 2048, 64 experts, top-4,
+# moe_intermediate 1024.
+GEMMA4_STYLE = MoeConfig(2048, 64, 4, 1024, 0, SCORING_SOFTMAX, True, False, name="gemma4-style")
 
 
 @dataclass
@@ -113,6 +117,15 @@ def host_block(cfg: MoeConfig, seed: int, bias_std: Optional[float] = None) -> B
         if cfg.has_shared_gate:
             bw.shared_expert_gate = _qweight(rng, 1, H, gs, bits)
     return bw
+
+
+def host_gemma4_scales(cfg: MoeConfig, seed: int):
+    """The Gemma4 router's `scale` [H] and `per_expert_scale` [E] (bf16 bits), each
+    ~ U(0.5, 1.5) (seeded)."""
+    rng = np.random.default_rng([seed, 4])
+    rs = f32_to_bf16_bits(rng.uniform(0.5, 1.5, cfg.hidden).astype(np.float32))
+    pes = f32_to_bf16_bits(rng.uniform(0.5, 1.5, cfg.num_experts).astype(np.float32))
+    return rs, pes
 
 
 def host_x(seed: int, T: int, H: int) -> np.ndarray:

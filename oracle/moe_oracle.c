@@ -737,3 +737,216 @@ done:
     free(gl);
     return rc;
 }
+
+/* ------------------------------------------------------------------------- */
+/* Gemma4 MoE block (crates/mlx-models/src/gemma4.rs)                        */
+/* ------------------------------------------------------------------------- */
+
+/* f32 rows in lane-major order (x_to_lane_major for f32 input). */
+static void xf_to_lane_major(const float* x, int64_t K, float* xt) {
+    const int64_t nr = lane_rounds(K), nchunks = K / 32;
+    for (int64_t r = 0; r < nr; ++r)
+        for (int j = 0; j < 32; ++j)
+            for (int l = 0; l < 32; ++l) {
+                const int64_t c = l + 32 * r;
+                xt[(r * 32 + j) * 32 + l] = (c < nchunks) ? x[32 * c + j] : 0.0f;
+            }
+}
+
+typedef struct {
+    const float* xt;
+    const uint32_t* w;
+    const uint16_t *s, *b;
+    float* out;
+    const int64_t *cnt, *order;
+    int64_t x_repeat, K, N;
+    int gs, bits;
+    int64_t nr, L, wpr, gpr;
+} gqmmf_ctx;
+
+static void gqmmf_rows(int64_t r0, int64_t r1, void* vctx, void* scratch) {
+    const gqmmf_ctx* c = (const gqmmf_ctx*)vctx;
+    float* wt = (float*)scratch;
+    for (int64_t row = r0; row < r1; ++row) {
+        const int64_t e = row / c->N, n = row % c->N;
+        if (c->cnt[e + 1] == c->cnt[e]) continue;
+        w_to_lane_major(c->w + row * c->wpr, c->s + row * c->gpr, c->b ? c->b + row * c->gpr : NULL,
+                        c->K, c->gs, c->bits, wt);
+        for (int64_t p = c->cnt[e]; p < c->cnt[e + 1]; ++p) {
+            const int64_t i = c->order[p];
+            c->out[i * c->N + n] = dot_lane_major(c->xt + (i / c->x_repeat) * c->L, wt, c->nr);
+        }
+    }
+}
+
+/* out[i, n] (f32, not rounded) = dot(x[i / x_repeat] (f32), W[rhs[i], n]): gather_qmm with
+ * an f32 x, whose output MLX keeps in f32 (the Gemma4 down projection, gemma4.rs:1050). */
+static int gather_qmm_f32(const float* x, int64_t K, int64_t x_repeat, const uint32_t* w, const uint16_t* s,
+                          const uint16_t* b, int64_t E, int64_t N, const uint32_t* rhs, int64_t batch, int gs,
+                          int bits, float* out, int nthreads) {
+    int rc = check_q(K, gs, bits);
+    if (rc) return rc;
+    const int64_t xrows = (batch + x_repeat - 1) / x_repeat;
+    const int64_t nr = lane_rounds(K), L = nr * 32 * 32;
+    float* xt = (float*)malloc(sizeof(float) * L * xrows);
+    int64_t* cnt = (int64_t*)calloc((size_t)E + 1, sizeof(int64_t));
+    int64_t* order = (int64_t*)malloc(sizeof(int64_t) * batch);
+    int64_t* cur = (int64_t*)malloc(sizeof(int64_t) * (E + 1));
+    if (!xt || !cnt || !order || !cur) {
+        free(xt);
+        free(cnt);
+        free(order);
+        free(cur);
+        return -10;
+    }
+    for (int64_t r = 0; r < xrows; ++r) xf_to_lane_major(x + r * K, K, xt + r * L);
+    for (int64_t i = 0; i < batch; ++i) cnt[rhs[i] + 1]++;
+    for (int64_t e = 0; e < E; ++e) cnt[e + 1] += cnt[e];
+    memcpy(cur, cnt, sizeof(int64_t) * (E + 1));
+    for (int64_t i = 0; i < batch; ++i) order[cur[rhs[i]]++] = i;
+    gqmmf_ctx c = {xt, w, s, b, out, cnt, order, x_repeat, K, N, gs, bits, nr, L, K * bits / 32, K / gs};
+    parallel_for(E * N, 4, nthreads, sizeof(float) * L, gqmmf_rows, &c);
+    free(xt);
+    free(cnt);
+    free(order);
+    free(cur);
+    return 0;
+}
+
+/* Top-k of f32 keys in the order of topk_row (key desc, index asc, NaN last). */
+static void topk_row_f32(const float* key, int64_t E, int k, uint32_t* sel) {
+    for (int j = 0; j < k; ++j) {
+        int64_t best = -1;
+        float bv = 0.0f;
+        for (int64_t e = 0; e < E; ++e) {
+            int taken = 0;
+            for (int jj = 0; jj < j; ++jj)
+                if (sel[jj] == (uint32_t)e) taken = 1;
+            if (taken) continue;
+            const float v = key[e];
+            const int better = best < 0 || (isnan(bv) && !isnan(v)) || (!isnan(v) && v > bv);
+            if (better) {
+                best = e;
+                bv = v;
+            }
+        }
+        sel[j] = (uint32_t)best;
+    }
+}
+
+/*
+ * The Gemma4 SparseMoeBlock::forward (gemma4.rs:1063-1085) op by op:
+ *   Router::forward (:906-936): h = fast_rms_norm(x, ones, 1e-6) (bf16), then
+ *     h * from_float(hidden^-0.5) * scale — from_float is a 0-d f32 array, so h becomes
+ *     f32 (the 0-d array is f32: crates/mlx-core/src/array.rs:82-87) and the router
+ *     continues in f32: logits = quantized_matmul(h) (f32), probs = softmax(logits) (f32),
+ *     top-k indices of -logits (argpartition), w = probs[idx] / sum_j probs[idx_j],
+ *     w *= per_expert_scale[idx];
+ *   SwitchGlu::forward (:1045-1052): up = gather_qmm(x) and gate = gather_qmm(x) (bf16),
+ *     hidden = gelu_approx(gate) * up in f32 (gelu_approx :308-322 multiplies by 0-d f32
+ *     arrays: 0.5 * (g * (1 + tanh(sqrt(2/pi) * (g + 0.044715 * g^3)))), power as powf),
+ *     y = gather_qmm(hidden) in f32;
+ *   the block: out = sum_j y_j * w_j (f32 products, sum in j order).
+ * out [T, H] f32; idx_out [T, k] and weights_out [T, k] (f32) optional.
+ */
+int oracle_gemma4_block_forward(const oracle_block_config* cfg, const oracle_block_weights* wt,
+                                const uint16_t* router_scale, const uint16_t* per_expert_scale,
+                                const uint16_t* x, int64_t T, float* out, uint32_t* idx_out,
+                                float* weights_out, int nthreads) {
+    const int64_t H = cfg->hidden, E = cfg->num_experts, I = cfg->moe_inter;
+    const int k = cfg->top_k, gs = cfg->group_size, bits = cfg->bits;
+    if (T == 0) return 0;
+    if (k <= 0 || k > E) return -6;
+    const int64_t P = T * k;
+    int rc = 0;
+    uint16_t* ones = (uint16_t*)malloc(sizeof(uint16_t) * H);
+    uint16_t* hn = (uint16_t*)malloc(sizeof(uint16_t) * T * H);
+    float* hf = (float*)malloc(sizeof(float) * T * H);
+    float* logits = (float*)malloc(sizeof(float) * T * E);
+    float* ex = (float*)malloc(sizeof(float) * E);
+    uint32_t* idx = (uint32_t*)malloc(sizeof(uint32_t) * P);
+    float* w = (float*)malloc(sizeof(float) * P);
+    uint16_t* g = (uint16_t*)malloc(sizeof(uint16_t) * P * I);
+    uint16_t* u = (uint16_t*)malloc(sizeof(uint16_t) * P * I);
+    float* hid = (float*)malloc(sizeof(float) * P * I);
+    float* y = (float*)malloc(sizeof(float) * P * H);
+    if (!ones || !hn || !hf || !logits || !ex || !idx || !w || !g || !u || !hid || !y) {
+        rc = -10;
+        goto gdone;
+    }
+    for (int64_t i = 0; i < H; ++i) ones[i] = 0x3f80; /* bf16 1.0 */
+    rc = oracle_rms_norm(x, ones, 1e-6f, T, H, hn, nthreads);
+    if (rc) goto gdone;
+    {
+        const float root = (float)(1.0 / sqrt((double)H)); /* (hidden_size as f32).powf(-0.5) */
+        for (int64_t i = 0; i < T * H; ++i) hf[i] = (bf2f(hn[i]) * root) * bf2f(router_scale[i % H]);
+    }
+    {
+        /* logits[t, e] = canonical dot of the f32 row with router row e */
+        /* as a gather_qmm of the T*E pairs (t, e) over "experts" of one row each: pair
+         * i = t*E + e reads f32 row t (x_repeat = E) against router row e */
+        uint32_t* rr = (uint32_t*)malloc(sizeof(uint32_t) * T * E);
+        if (!rr) {
+            rc = -10;
+            goto gdone;
+        }
+        for (int64_t i = 0; i < T * E; ++i) rr[i] = (uint32_t)(i % E);
+        rc = gather_qmm_f32(hf, H, E, wt->router.w, wt->router.s, wt->router.b, E, 1, rr, T * E, gs, bits,
+                            logits, nthreads);
+        free(rr);
+        if (rc) goto gdone;
+    }
+    for (int64_t t = 0; t < T; ++t) {
+        const float* l = logits + t * E;
+        float m = -INFINITY;
+        for (int64_t e = 0; e < E; ++e) m = l[e] > m ? l[e] : m;
+        for (int64_t e = 0; e < E; ++e) ex[e] = oracle_exp(l[e] - m);
+        const float s = sum_canonical(ex, E);
+        topk_row_f32(l, E, k, idx + t * k);
+        float d = 0.0f;
+        for (int j = 0; j < k; ++j) d = d + ex[idx[t * k + j]] / s;
+        for (int j = 0; j < k; ++j) {
+            const uint32_t e = idx[t * k + j];
+            w[t * k + j] = ((ex[e] / s) / d) * bf2f(per_expert_scale[e]);
+        }
+    }
+    rc = oracle_gather_qmm(x, H, k, NULL, wt->up.w, wt->up.s, wt->up.b, E, I, idx, P, gs, bits, u, nthreads);
+    if (rc) goto gdone;
+    rc = oracle_gather_qmm(x, H, k, NULL, wt->gate.w, wt->gate.s, wt->gate.b, E, I, idx, P, gs, bits, g,
+                           nthreads);
+    if (rc) goto gdone;
+    {
+        const float kS2P = sqrtf(2.0f / 3.14159265358979323846f); /* (2.0f32 / PI).sqrt() */
+        const float kC = 0.044715f;
+        for (int64_t i = 0; i < P * I; ++i) {
+            const float gv = bf2f(g[i]);
+            const float x3 = powf(gv, 3.0f);
+            const float inner = (gv + x3 * kC) * kS2P;
+            const float gate = 1.0f + tanhf(inner);
+            hid[i] = (0.5f * (gv * gate)) * bf2f(u[i]);
+        }
+    }
+    rc = gather_qmm_f32(hid, I, 1, wt->down.w, wt->down.s, wt->down.b, E, H, idx, P, gs, bits, y, nthreads);
+    if (rc) goto gdone;
+    for (int64_t t = 0; t < T; ++t)
+        for (int64_t h = 0; h < H; ++h) {
+            float acc = 0.0f;
+            for (int j = 0; j < k; ++j) acc = acc + y[(t * k + j) * H + h] * w[t * k + j];
+            out[t * H + h] = acc;
+        }
+    if (idx_out) memcpy(idx_out, idx, sizeof(uint32_t) * P);
+    if (weights_out) memcpy(weights_out, w, sizeof(float) * P);
+gdone:
+    free(ones);
+    free(hn);
+    free(hf);
+    free(logits);
+    free(ex);
+    free(idx);
+    free(w);
+    free(g);
+    free(u);
+    free(hid);
+    free(y);
+    return rc;
+}

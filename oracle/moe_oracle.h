@@ -112,6 +112,14 @@ int oracle_block_forward(const oracle_block_config* cfg, const oracle_block_weig
                          const uint16_t* x, int64_t T, uint16_t* out, uint32_t* idx_out,
                          uint16_t* weights_out, int nthreads);
 
+/* The Gemma4 MoE block (gemma4.rs:1063-1085): f32 router input, f32 logits, top-k by
+ * logit, f32 weights softmax[idx] / sum * per_expert_scale[idx], GELU-tanh SwitchGLU with
+ * an f32 hidden and f32 down outputs; out [T, H] f32. shared_inter is ignored (none). */
+int oracle_gemma4_block_forward(const oracle_block_config* cfg, const oracle_block_weights* wt,
+                                const uint16_t* router_scale, const uint16_t* per_expert_scale,
+                                const uint16_t* x, int64_t T, float* out, uint32_t* idx_out,
+                                float* weights_out, int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -78,6 +78,9 @@ def lib():
         L.oracle_block_forward.argtypes = [C.POINTER(_Cfg), C.POINTER(_Wts), C.c_void_p, C.c_int64,
                                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
         L.oracle_swiglu.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]
+        L.oracle_gemma4_block_forward.argtypes = [C.POINTER(_Cfg), C.POINTER(_Wts), C.c_void_p, C.c_void_p,
+                                                  C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                  C.c_int]
         _lib = L
     return _lib
 
@@ -230,6 +233,23 @@ def block_forward(block, x, nthreads=0):
     w = np.empty((T, K), np.uint16)
     _check(lib().oracle_block_forward(C.byref(kp.cfg), C.byref(kp.wts), _p(x), T, _p(out),
                                       _p(idx), _p(w), nthreads), "oracle_block_forward")
+    return out, idx, w
+
+
+def gemma4_block_forward(block, router_scale, per_expert_scale, x, nthreads=0):
+    """The Gemma4 MoE block (gemma4.rs:1063-1085). Returns (out [T,H] f32, idx [T,k] u32,
+    weights [T,k] f32)."""
+    kp = _pack(block)
+    x = _c(x, np.uint16)
+    rs = _c(router_scale, np.uint16)
+    pes = _c(per_expert_scale, np.uint16)
+    T, H = x.shape
+    K = block.config.top_k
+    out = np.empty((T, H), np.float32)
+    idx = np.empty((T, K), np.uint32)
+    w = np.empty((T, K), np.float32)
+    _check(lib().oracle_gemma4_block_forward(C.byref(kp.cfg), C.byref(kp.wts), _p(rs), _p(pes), _p(x), T,
+                                             _p(out), _p(idx), _p(w), nthreads), "oracle_gemma4_block_forward")
     return out, idx, w
 
 

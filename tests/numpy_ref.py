@@ -122,3 +122,31 @@ def block_forward(bw: S.BlockWeights, x_bits):
             ys = bf(ys * gate)
         out = bf(out + ys)
     return out, idx, w
+
+
+def gemma4_block(bw: S.BlockWeights, router_scale_bits, pes_bits, x_bits):
+    """The Gemma4 block (gemma4.rs:906-936, 1045-1085) in float64 except where the
+    reference rounds to bf16 (the RMSNorm output, the gate/up gather_qmm outputs)."""
+    c = bw.config
+    x = f(x_bits)
+    ms = np.mean(x * x, axis=-1, keepdims=True)
+    hn = bf(x / np.sqrt(ms + 1e-6))
+    h = hn * (1.0 / np.sqrt(c.hidden)) * f(router_scale_bits)
+    logits = h @ dequant(bw.router, c.group_size, c.bits).T
+    m = logits.max(axis=-1, keepdims=True)
+    p = np.exp(logits - m)
+    p = p / p.sum(axis=-1, keepdims=True)
+    idx = np.argsort(-logits, axis=-1, kind="stable")[:, :c.top_k]
+    w = np.take_along_axis(p, idx, -1)
+    w = w / w.sum(-1, keepdims=True) * f(pes_bits)[idx]
+    T, k = idx.shape
+    out = np.zeros((T, c.hidden))
+    for t in range(T):
+        for j in range(k):
+            e = idx[t, j]
+            g = bf(x[t] @ dequant(S.QWeight(bw.gate.w[e], bw.gate.scales[e], bw.gate.biases[e])).T)
+            u = bf(x[t] @ dequant(S.QWeight(bw.up.w[e], bw.up.scales[e], bw.up.biases[e])).T)
+            gl = 0.5 * g * (1.0 + np.tanh(np.sqrt(2.0 / np.pi) * (g + 0.044715 * g ** 3)))
+            y = (gl * u) @ dequant(S.QWeight(bw.down.w[e], bw.down.scales[e], bw.down.biases[e])).T
+            out[t] += y * w[t, j]
+    return out, idx.astype(np.uint32), w

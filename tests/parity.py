@@ -66,3 +66,20 @@ def assert_close(y_bits, ref_bits, what="", ulp_tol=ULP_TOL):
     assert m["mean_rel"] <= MEAN_REL_TOL, f"{what}: mean_rel {m}"
     assert not bad.any(), f"{what}: {int(bad.sum())} elements beyond 2e-2 + {ulp_tol:g} row ulps; {m}"
     return m
+
+
+def assert_close_f32(y, ref, what="", ulp_tol=ULP_TOL_TC):
+    """The bound of assert_close for f32 outputs (the Gemma4 block): mean_rel <= 1e-2 and
+    |y - ref| <= 2e-2 + ulp_tol bf16 ulps of the row's largest |ref|."""
+    y = np.asarray(y, dtype=np.float64)
+    r = np.asarray(ref, dtype=np.float64)
+    assert y.shape == r.shape, (y.shape, r.shape)
+    assert np.all(np.isfinite(y)), f"{what}: non-finite output"
+    d = np.abs(y - r)
+    mean_rel = float(d.mean() / np.abs(r).mean())
+    rowmax = np.max(np.abs(r), axis=-1, keepdims=True)
+    bad = d > ABS_TOL + ulp_tol * ulp_bf16(rowmax)
+    m = {"max_abs": float(d.max()), "mean_rel": mean_rel, "rms_ref": float(np.sqrt(np.mean(r * r)))}
+    assert mean_rel <= MEAN_REL_TOL, f"{what}: mean_rel {m}"
+    assert not bad.any(), f"{what}: {int(bad.sum())} elements beyond the bound; {m}"
+    return m

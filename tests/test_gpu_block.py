@@ -602,3 +602,36 @@ def test_decode_kernel_layer_step_vs_oracle(monkeypatch):
     torch.cuda.synchronize()
     y, _, _, _ = O.layer_ffn_forward(bw, x, nw, 1e-6)
     assert_close(dev_bits(out).reshape(y.shape), y, "decode kernel layer step")
+
+
+# ----------------------------------------------------------------------------------
+# the Gemma4 MoE variant (gemma4.rs Router + GELU SwitchGlu, f32 router and output)
+# ----------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("T", [1, 8, 64, 512, 2048])
+def test_gemma4_block_vs_oracle(T):
+    """moe_gemma4_block_forward against the oracle's restatement of the reference:
+    experts and f32 combine weights bit for bit (the router runs the canonical order on
+    the f32 router input, softmax and renormalisation in the same IEEE operations), the
+    f32 block output within the tolerance (the kernels round the GELU hidden and the
+    expert outputs to bf16; at T >= 512 most experts take the tcgen05 GEMM)."""
+    torch = _torch()
+    import oracle as O
+    from mlx_rs_b200.block import Gemma4MoeBlock
+    from gpu_util import to_dev
+    from parity import assert_close_f32
+    cfg = S.GEMMA4_STYLE
+    key = ("gemma4", cfg)
+    if key not in _BLOCKS:
+        bw = S.host_block(cfg, 7)
+        rs, pes = S.host_gemma4_scales(cfg, 7)
+        _BLOCKS[key] = (bw, rs, pes, Gemma4MoeBlock(S.to_device(bw, "cuda"), to_dev(rs), to_dev(pes)))
+    bw, rs, pes, blk = _BLOCKS[key]
+    x = S.host_x(1700 + T, T, cfg.hidden)
+    out, idx, w = blk.forward(to_dev(x), routing=True)
+    torch.cuda.synchronize()
+    y, ridx, rw = O.gemma4_block_forward(bw, rs, pes, x)
+    assert np.array_equal(idx.cpu().numpy().view(np.uint32), ridx), "experts differ"
+    assert np.array_equal(w.cpu().numpy().view(np.uint32), rw.view(np.uint32)), "combine weights differ"
+    assert out.dtype == torch.float32
+    assert_close_f32(out.cpu().numpy(), y, f"gemma4 T={T}")

@@ -196,3 +196,20 @@ def test_topk_nan_keys_rank_last_and_stay_distinct():
                      [two, nan, one, nan, nan, two]], np.uint16)
     idx = O.topk_rows(keys, 4)
     assert idx.tolist() == [[3, 1, 0, 2], [0, 1, 2, 3], [0, 5, 2, 1]]
+
+
+def test_gemma4_oracle_vs_numpy_restatement():
+    """The C oracle's Gemma4 block (f32 router cascade, top-k by logit, GELU SwitchGLU with
+    an f32 hidden) against the float64 restatement: same experts in the same order, weights
+    and outputs within f32 rounding."""
+    import numpy_ref as R
+    cfg = S.GEMMA4_STYLE
+    bw = S.host_block(cfg, 7)
+    rs, pes = S.host_gemma4_scales(cfg, 7)
+    x = S.host_x(3, 6, cfg.hidden)
+    y, idx, w = O.gemma4_block_forward(bw, rs, pes, x)
+    yr, idxr, wr = R.gemma4_block(bw, rs, pes, x)
+    assert np.array_equal(idx, idxr)
+    np.testing.assert_allclose(w, wr, rtol=1e-5)
+    rel = np.abs(y - yr).mean() / np.abs(yr).mean()
+    assert rel < 2e-6, rel
