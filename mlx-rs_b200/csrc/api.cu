@@ -235,6 +235,11 @@ int check_block(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights
   const void* ptrs[] = {w->router.w, w->gate.w, w->up.w, w->down.w};
   for (const void* p : ptrs)
     if (!aligned16(p)) return fail(ctx, MOE_ERR_INVALID, "%s: weight pointers must be 16-byte aligned", fn);
+  if (c->shared_inter > 0) {
+    const void* sp[] = {w->shared_gate.w, w->shared_up.w, w->shared_down.w};
+    for (const void* p : sp)
+      if (!aligned16(p)) return fail(ctx, MOE_ERR_INVALID, "%s: weight pointers must be 16-byte aligned", fn);
+  }
   return MOE_OK;
 }
 

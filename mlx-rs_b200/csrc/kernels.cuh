@@ -1,6 +1,7 @@
 // kernels.cuh — argument blocks and launchers of the MoE kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -162,6 +163,9 @@ struct TcGemmArgs {
   int max_tiles;              // grid.y
   int32_t* status;            // device word: nonzero after a bounded wait expired
   int ksplit;                 // grid.z: K splits into q.partial [ksplit][rows][N or 2N], 0/1 none
+  // TMA maps of the packed weights q.w0 / q.w1 ([num_experts * N rows][K / 8 words],
+  // box [128 rows][8 words]); filled by launch_tc_gemm
+  CUtensorMap wmap[2];
 };
 // Ordered reduction of split-K partials (q.partial, q.ksplit, q.part_rows) into q.out.
 cudaError_t launch_gemv_reduce(const QgemvArgs& q, bool gated, cudaStream_t st);

@@ -22,9 +22,17 @@
 //     the reference; the sigmoid from the hardware ex2/rcp approximations, which is why
 //     this path has its own tolerance against the oracle). Each warp transposes its
 //     32 x 32 tile through shared memory so that the outputs leave as 16-byte stores.
+//   * warp 17 streams the packed weights: per K step, one 2D TMA load
+//     (cp.async.bulk.tensor) of the [128 rows][32 bytes] tile of each matrix into a slot
+//     of a kPackSlots-deep ring (full: the TMA's bytes landed; empty: every producer
+//     warp read its words), so the producers dequantise from shared memory instead of
+//     waiting on global loads.
 // The shared-memory ring has kStages stages guarded by full/empty mbarriers. Every
-// mbarrier wait is bounded; on expiry the CTA records a status code and drains out.
-// No TMA and no cluster multicast are used.
+// mbarrier wait is bounded; on expiry the CTA records a status code and drains out (the
+// TMA warp waits for its copies in flight before the CTA exits). The TMA loads are plain
+// loads of this GPU's memory, never with cluster multicast.
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -42,7 +50,10 @@ constexpr int kParts = kProducers / kBM;    // producer threads per weight row (
 constexpr int kWords = 8 / kParts;          // packed words of a group each handles (2)
 constexpr int kColGroups = kProducers / 128;  // epilogue: warps sharing a TMEM lane quadrant
 constexpr int kMmaWarp = kProducers / 32;
-constexpr int kThreads = kProducers + 32;
+constexpr int kTmaWarp = kMmaWarp + 1;        // streams the packed weight tiles
+constexpr int kThreads = kProducers + 64;
+constexpr int kPackSlots = 4;                 // K steps of packed weights in flight
+constexpr int kPackTileBytes = kBM * 32;      // [128 rows][8 words] of one matrix, one K step
 constexpr uint64_t kWaitLimitNs = 200ull * 1000 * 1000;  // bound of one mbarrier wait (200 ms)
 
 // MODE 0: plain, 128 weight rows per CTA; 1: gated (gate and up rows); 2: plain, 256
@@ -53,9 +64,12 @@ struct TcCfg {
   static constexpr int kStages = MODE ? 3 : 4;
   static constexpr int kStageBytes = kMats * kATileBytes + kBTileBytes;
   static constexpr int kTmemCols = MODE ? 512 : 256;
-  // [stages][A tiles..., B tile] | full[S] empty[S] done | tmem base | xrow[kBN]
-  static constexpr int kBarOffset = kStages * kStageBytes;
-  static constexpr int kSmemBytes = kBarOffset + 8 * (2 * kStages + 1) + 16 + 4 * kBN + 1024;
+  // [stages][A tiles..., B tile] | [pack slots][matrices][128 rows][32 B] |
+  // full[S] empty[S] done pfull[P] pempty[P] | tmem base | xrow[kBN]
+  static constexpr int kPackOffset = kStages * kStageBytes;
+  static constexpr int kBarOffset = kPackOffset + kPackSlots * kMats * kPackTileBytes;
+  static constexpr int kNumBars = 2 * kStages + 1 + 2 * kPackSlots;
+  static constexpr int kSmemBytes = kBarOffset + 8 * kNumBars + 16 + 4 * kBN + 1024;
 };
 
 MOE_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -89,6 +103,20 @@ MOE_DEV bool mbar_wait(uint32_t bar, uint32_t parity) {
   while (!mbar_try_wait(bar, parity))
     if (global_ns() - t0 > kWaitLimitNs) return false;
   return true;
+}
+
+MOE_DEV void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+// 2D tiled TMA load of the box at (x, y) of the tensor map into shared memory, completing
+// on bar. A plain load: no cluster multicast (this kernel also runs under expert
+// parallelism).
+MOE_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
 }
 
 MOE_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
@@ -243,7 +271,7 @@ struct RowMap {
 }  // namespace
 
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
+__global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_constant__ TcGemmArgs ta) {
   using C = TcCfg<MODE>;
   constexpr bool GATED = MODE == 1;
   constexpr int kRowsPerCta = MODE == 2 ? 2 * kBM : kBM;
@@ -254,12 +282,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
   const uint32_t bar_full = sbase + C::kBarOffset;
   const uint32_t bar_empty = bar_full + 8 * C::kStages;
   const uint32_t bar_done = bar_empty + 8 * C::kStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kBarOffset + 8 * (2 * C::kStages + 1));
-  int32_t* xrow_s = reinterpret_cast<int32_t*>(smem + C::kBarOffset + 8 * (2 * C::kStages + 1) + 16);
+  const uint32_t bar_pfull = bar_done + 8;                  // packed slot landed (TMA bytes)
+  const uint32_t bar_pempty = bar_pfull + 8 * kPackSlots;   // packed slot read by every producer warp
+  const uint32_t pack_s = sbase + C::kPackOffset;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kBarOffset + 8 * C::kNumBars);
+  int32_t* xrow_s = reinterpret_cast<int32_t*>(smem + C::kBarOffset + 8 * C::kNumBars + 16);
   __shared__ int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int K = a.K, N = a.N, Gtot = K >> 6, wpr = K >> 3;
+  const int K = a.K, N = a.N, Gtot = K >> 6;
   // split-K (blockIdx.z): this CTA accumulates K steps [G0, G0 + G) of the Gtot
   const int ksp = ta.ksplit > 1 ? ta.ksplit : 1;
   const int spk = (Gtot + ksp - 1) / ksp;
@@ -302,6 +333,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
       mbar_init(bar_empty + 8 * s, 1);
     }
     mbar_init(bar_done, 1);
+    for (int i = 0; i < kPackSlots; ++i) {
+      mbar_init(bar_pfull + 8 * i, 1);
+      mbar_init(bar_pempty + 8 * i, kMmaWarp);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   for (int i = tid; i < kBN; i += kThreads) xrow_s[i] = i < ntok ? (int32_t)rm.xrow(tbeg + i) : -1;
   if (warp == kMmaWarp) {
@@ -320,30 +356,26 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
     const int p = tid;               // 0..kProducers-1
     const int part = p % kParts;     // which kWords words (8 elements each) of the row's group
     const int row = p / kParts;      // weight row within the tile
-    const uint32_t* wrow[C::kMats];
     const uint16_t* srow[C::kMats];
     const uint16_t* brow[C::kMats];
 #pragma unroll
     for (int m = 0; m < C::kMats; ++m) {
       const size_t grow = (size_t)e * N + n0 + (MODE == 2 ? m * kBM : 0) + row;
       const bool second = GATED && m;
-      const uint32_t* W = second ? a.w1 : a.w0;
       const uint16_t* S = second ? a.s1 : a.s0;
       const uint16_t* B = second ? a.b1 : a.b0;
-      wrow[m] = W + grow * wpr + (size_t)G0 * 8 + part * kWords;
       srow[m] = S + grow * Gtot + G0;
       brow[m] = B ? B + grow * Gtot + G0 : nullptr;
     }
-    // register ring of packed weights + (scale | bias << 16), kRing - 1 stages ahead
-    static_assert(kWords == 2, "the loads below move 2 words per matrix");
+    // register ring of (scale | bias << 16), kRing - 1 stages ahead; the packed weights
+    // come from the slots the TMA warp fills (this thread: 8 bytes of row `row`)
+    static_assert(kWords == 2, "the slot reads below move 2 words per matrix");
     constexpr int kRing = 4;
-    uint2 wr[kRing][C::kMats];
     uint32_t sr[kRing][C::kMats];
     auto load_w = [&](int slot3, int kk) {
       if (kk < G) {
 #pragma unroll
         for (int m = 0; m < C::kMats; ++m) {
-          wr[slot3][m] = __ldg(reinterpret_cast<const uint2*>(wrow[m] + (size_t)kk * 8));
           const uint32_t sv = __ldg(srow[m] + kk);
           const uint32_t bv = brow[m] ? __ldg(brow[m] + kk) : 0u;
           sr[slot3][m] = sv | (bv << 16);
@@ -380,12 +412,27 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
         if (kk < G && ok) {
           const int s = kk % C::kStages;
           const uint32_t st = sbase + s * C::kStageBytes;
+          // the packed weights of K step kk: slot kk % kPackSlots, then release the slot
+          const int ps = kk % kPackSlots;
+          if (!__all_sync(0xffffffffu, mbar_wait(bar_pfull + 8 * ps, (kk / kPackSlots) & 1))) {
+            ok = false;  // warp-uniform: the whole warp leaves together
+            if (lane == 0) atomicOr(&abort_flag, 16);
+            break;
+          }
+          uint2 wr[C::kMats];
+#pragma unroll
+          for (int m = 0; m < C::kMats; ++m) {
+            const uint32_t src = pack_s + (uint32_t)((ps * C::kMats + m) * kPackTileBytes + row * 32 + part * 8);
+            asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(wr[m].x), "=r"(wr[m].y) : "r"(src) : "memory");
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_pempty + 8 * ps);
           // dequantise A(kk) into stage s (freed: its empty barrier was awaited when B(kk) was issued)
 #pragma unroll
           for (int m = 0; m < C::kMats; ++m) {
             const uint32_t sv = sr[r3][m] & 0xffffu, bv = sr[r3][m] >> 16;
             const uint32_t s2 = sv | (sv << 16), b2 = bv | (bv << 16);
-            const uint2 wv = wr[r3][m];
+            const uint2 wv = wr[m];
             const uint32_t ws[2] = {wv.x, wv.y};
 #pragma unroll
             for (int j = 0; j < kWords; ++j) {
@@ -406,9 +453,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
           if (kn < G) {
             const int sn = kn % C::kStages;
             const int use = kn / C::kStages;  // this is use number `use` of stage sn
-            if (use > 0 && !mbar_wait(bar_empty + 8 * sn, (use - 1) & 1)) {
-              ok = false;
-              atomicOr(&abort_flag, 1);
+            if (use > 0 && !__all_sync(0xffffffffu, mbar_wait(bar_empty + 8 * sn, (use - 1) & 1))) {
+              ok = false;  // warp-uniform (the slot reads above synchronise the warp)
+              if (lane == 0) atomicOr(&abort_flag, 1);
             }
             if (ok) issue_b(kn);
           } else {
@@ -511,8 +558,37 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
         }
       }
     }
+  } else if (warp == kTmaWarp) {
+    // ================= packed weights by TMA (one lane) =================
+    // K step kk: the [128 rows][8 words] tile of each matrix at (x = (G0 + kk) * 8 words,
+    // y = e * N + n0 (+ 128 for the second accumulator of mode 2)) into slot kk % kPackSlots,
+    // once every producer warp has released the slot's previous use
+    if (lane == 0) {
+      int issued = 0;
+      bool ok = true;
+      for (int kk = 0; kk < G && ok; ++kk) {
+        const int ps = kk % kPackSlots;
+        if (kk >= kPackSlots && !mbar_wait(bar_pempty + 8 * ps, ((kk / kPackSlots) - 1) & 1)) {
+          ok = false;
+          atomicOr(&abort_flag, 32);
+          break;
+        }
+        mbar_expect_tx(bar_pfull + 8 * ps, C::kMats * kPackTileBytes);
+#pragma unroll
+        for (int m = 0; m < C::kMats; ++m) {
+          const int y = e * N + n0 + (MODE == 2 ? m * kBM : 0);
+          tma_load_2d(pack_s + (uint32_t)((ps * C::kMats + m) * kPackTileBytes), &ta.wmap[GATED ? m : 0],
+                      (G0 + kk) * 8, y, bar_pfull + 8 * ps);
+        }
+        issued = kk + 1;
+      }
+      // no copy may still be landing when the CTA exits (producers that gave up early
+      // left slots unconsumed): wait for the last copy issued into each slot
+      for (int kk = issued - kPackSlots < 0 ? 0 : issued - kPackSlots; kk < issued; ++kk)
+        if (!mbar_wait(bar_pfull + 8 * (kk % kPackSlots), (kk / kPackSlots) & 1)) atomicOr(&abort_flag, 32);
+    }
   } else if (lane == 0) {
-    // ================= MMA issuer (warp 8, one lane) =================
+    // ================= MMA issuer (warp 16, one lane) =================
     const uint32_t idesc = idesc_bf16(nmma);
     bool ok = true;
     for (int kk = 0; kk < G; ++kk) {
@@ -554,6 +630,36 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemmArgs ta) {
   }
 }
 
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime (no link
+// against libcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// The packed weights [rows][K / 8] uint32 as a 2D tensor map with [128 rows][8 words]
+// boxes (one K step of one 128-row tile; 32-byte inner extent, 16-byte aligned rows).
+static cudaError_t encode_weight_map(CUtensorMap* map, const uint32_t* w, int64_t rows, int K) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  if (reinterpret_cast<uintptr_t>(w) & 15) return cudaErrorInvalidValue;
+  const cuuint64_t dims[2] = {(cuuint64_t)(K / 8), (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(K / 8) * 4};
+  const cuuint32_t box[2] = {8, (cuuint32_t)kBM};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(w), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 template <int MODE>
 static cudaError_t launch_tc_t(const TcGemmArgs& a, cudaStream_t st) {
   using C = TcCfg<MODE>;
@@ -570,11 +676,20 @@ static cudaError_t launch_tc_t(const TcGemmArgs& a, cudaStream_t st) {
   return launch_k(tc_gemm_kernel<MODE>, grid, dim3(kThreads), (size_t)C::kSmemBytes, st, a);
 }
 
-cudaError_t launch_tc_gemm(const TcGemmArgs& a, bool gated, cudaStream_t st) {
-  if (a.max_tiles <= 0) return cudaSuccess;
-  if (a.q.N % kBM != 0 || a.q.K % kBK != 0) return cudaErrorInvalidValue;
-  cudaError_t err = gated ? launch_tc_t<1>(a, st)
-                          : (a.q.N % (2 * kBM) == 0 ? launch_tc_t<2>(a, st) : launch_tc_t<0>(a, st));
+cudaError_t launch_tc_gemm(const TcGemmArgs& a0, bool gated, cudaStream_t st) {
+  if (a0.max_tiles <= 0) return cudaSuccess;
+  if (a0.q.N % kBM != 0 || a0.q.K % kBK != 0) return cudaErrorInvalidValue;
+  TcGemmArgs a = a0;
+  const int64_t rows = (int64_t)(a.tile_start ? a.num_experts : 1) * a.q.N;
+  cudaError_t err = encode_weight_map(&a.wmap[0], a.q.w0, rows, a.q.K);
+  if (err != cudaSuccess) return err;
+  if (gated) {
+    err = encode_weight_map(&a.wmap[1], a.q.w1, rows, a.q.K);
+    if (err != cudaSuccess) return err;
+  } else {
+    a.wmap[1] = a.wmap[0];
+  }
+  err = gated ? launch_tc_t<1>(a, st) : (a.q.N % (2 * kBM) == 0 ? launch_tc_t<2>(a, st) : launch_tc_t<0>(a, st));
   if (err != cudaSuccess || a.ksplit <= 1) return err;
   QgemvArgs r = a.q;
   r.ksplit = a.ksplit;
