@@ -211,6 +211,18 @@ int moe_block_route(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_w
                     uint32_t* perm);
 
 /*
+ * The router linear of a block alone: logits[T, n] (bf16, n = num_experts, plus one
+ * column for the shared_expert_gate row when shared_inter > 0 and has_shared_gate), the
+ * quantized_matmul of Linear::forward (crates/mlx-nn/src/linear.rs:117-128) on the gate
+ * weight (qwen3_moe_python_port.rs:436, lfm2_moe_python_port.rs:559) and on
+ * shared_expert_gate (qwen3_moe_python_port.rs:475-476), with the same canonical fp32
+ * order as the routing of moe_block_forward (bit-identical logits). Reads only
+ * wts->router and wts->shared_expert_gate.
+ */
+int moe_block_router_logits(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts,
+                            const void* x, int64_t T, void* logits);
+
+/*
  * moe_block_forward with CUDA events between its stages; blocks until the block has
  * run. stage_ms[8] receives the device time of: router, top-k, grouping, gate/up,
  * down, shared gate/up, shared down, combine; n_active (optional) the number of

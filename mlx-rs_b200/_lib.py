@@ -89,6 +89,8 @@ SIGNATURES = {
     "moe_block_profile": (C.c_int, [C.c_void_p, C.POINTER(BlockConfig), C.POINTER(BlockWeights),
                                     C.c_void_p, C.c_int64, C.c_void_p, C.POINTER(C.c_float),
                                     C.POINTER(C.c_int32)]),
+    "moe_block_router_logits": (C.c_int, [C.c_void_p, C.POINTER(BlockConfig), C.POINTER(BlockWeights),
+                                          C.c_void_p, C.c_int64, C.c_void_p]),
     "moe_block_route": (C.c_int, [C.c_void_p, C.POINTER(BlockConfig), C.POINTER(BlockWeights),
                                   C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p,
                                   C.c_void_p]),

@@ -122,6 +122,19 @@ class _Block:
         names = ("router", "topk", "group", "gate_up", "down", "shared_gate_up", "shared_down", "combine")
         return out, dict(zip(names, list(ms))), int(na.value)
 
+    def router_logits(self, x: torch.Tensor) -> torch.Tensor:
+        """Router logits [T, n] bf16 (n = num_experts, plus the shared_expert_gate column
+        when the block has one): the gate Linear of qwen3_moe_python_port.rs:436."""
+        H, E = self.config.hidden, self.config.num_experts
+        n = E + (1 if self.config.shared_inter > 0 and self.config.has_shared_gate else 0)
+        T = x.numel() // H
+        logits = torch.empty(T, n, dtype=torch.bfloat16, device=x.device)
+        ctx = _ctx(x)
+        rc = library().moe_block_router_logits(ctx.handle, C.byref(self._cfg), C.byref(self._wts), _ptr(x), T,
+                                               _ptr(logits))
+        ctx.check("moe_block_router_logits", rc)
+        return logits
+
     def route(self, x: torch.Tensor):
         """(idx [T,k] int32, weights [T,k] bf16, offsets [E+1] int32, perm [T*k] int32)."""
         H, E, k = self.config.hidden, self.config.num_experts, self.config.top_k

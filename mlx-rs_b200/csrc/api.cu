@@ -239,6 +239,8 @@ int check_block(moe_ctx* ctx, const moe_block_config* c, const moe_block_weights
     const void* sp[] = {w->shared_gate.w, w->shared_up.w, w->shared_down.w};
     for (const void* p : sp)
       if (!aligned16(p)) return fail(ctx, MOE_ERR_INVALID, "%s: weight pointers must be 16-byte aligned", fn);
+    if (c->has_shared_gate && !aligned16(w->shared_expert_gate.w))
+      return fail(ctx, MOE_ERR_INVALID, "%s: weight pointers must be 16-byte aligned", fn);
   }
   return MOE_OK;
 }
@@ -1008,6 +1010,36 @@ int moe_block_route(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_w
     MOE_CUDA(ctx, cudaMemcpyAsync(offsets, ws.offsets, (cfg->num_experts + 1) * 4, cudaMemcpyDeviceToDevice,
                                   ctx->stream));
   if (perm) MOE_CUDA(ctx, cudaMemcpyAsync(perm, ws.perm, P * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  return MOE_OK;
+}
+
+int moe_block_router_logits(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts,
+                            const void* x, int64_t T, void* logits) {
+  if (!ctx) return MOE_ERR_INVALID;
+  ctx->last_error.clear();
+  const char* fn = "moe_block_router_logits";
+  if (!cfg) return fail(ctx, MOE_ERR_INVALID, "%s: null config", fn);
+  int rc = check_quant(ctx, fn, cfg->hidden, cfg->group_size, cfg->bits);
+  if (rc) return rc;
+  if (cfg->num_experts <= 0 || cfg->num_experts > 512)
+    return fail(ctx, MOE_ERR_UNSUPPORTED, "%s: num_experts=%d (supported 1..512)", fn, cfg->num_experts);
+  if (!wts || !wts->router.w || !wts->router.scales || !aligned16(wts->router.w))
+    return fail(ctx, MOE_ERR_INVALID, "%s: router weight missing or not 16-byte aligned", fn);
+  const bool gate_row = cfg->shared_inter > 0 && cfg->has_shared_gate;
+  if (gate_row && (!wts->shared_expert_gate.w || !wts->shared_expert_gate.scales ||
+                   !aligned16(wts->shared_expert_gate.w)))
+    return fail(ctx, MOE_ERR_INVALID, "%s: shared_expert_gate weight missing or not 16-byte aligned", fn);
+  if (T < 0 || T > (INT32_MAX / 64)) return fail(ctx, MOE_ERR_INVALID, "%s: bad T", fn);
+  if (T == 0) return MOE_OK;
+  if (!x || !logits || !aligned16(x)) return fail(ctx, MOE_ERR_INVALID, "%s: x (16-byte aligned) and logits required", fn);
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
+  BlockWs ws{};
+  ws.logits = static_cast<uint16_t*>(logits);
+  moe::RouterArgs ra;
+  moe::TopkArgs ta;
+  route_args(cfg, wts, x, T, ws, ra, ta);
+  MOE_CUDA(ctx, moe::launch_router(ra, ctx->stream));
   return MOE_OK;
 }
 

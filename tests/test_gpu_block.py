@@ -160,6 +160,31 @@ def test_prefill_qwen3_skewed_T4096_all_rows():
     _live_full(cfg, 2, 4096, bias_std=2.0)
 
 
+@pytest.mark.parametrize("cname,seed,T", [
+    ("QWEN3_30B_A3B", 2, 1), ("QWEN3_30B_A3B", 2, 64), ("QWEN3_30B_A3B", 2, 65),
+    ("QWEN3_30B_A3B", 2, 1001), ("QWEN3_30B_A3B", 2, 4096),
+    ("QWEN15_MOE_A27B", 0, 77), ("QWEN15_MOE_A27B", 0, 203), ("QWEN15_MOE_A27B", 0, 512),
+    ("LFM2_8B_A1B", 3, 1024)])
+def test_router_logits_bit_exact(cname, seed, T):
+    """moe_block_router_logits against the oracle's router logits (and, with a shared
+    expert gate, its quantized_matmul of shared_expert_gate), bit for bit, on every
+    token: the small-batch router kernels (T <= 64) and the shared-memory one (larger
+    batches, including ragged last token groups)."""
+    import oracle as O
+    from gpu_util import dev_bits, to_dev
+    cfg = getattr(S, cname)
+    bw, blk = _block(cfg, seed)
+    x = S.host_x(seed, T, cfg.hidden)
+    got = dev_bits(blk.router_logits(to_dev(x)))
+    _, _, logits, _ = O.route(bw, x)
+    E = cfg.num_experts
+    assert np.array_equal(got[:, :E], logits), f"{cname} T={T}: router logits differ"
+    if cfg.shared_inter > 0 and cfg.has_shared_gate:
+        g = bw.shared_expert_gate
+        ref = O.qmm(x, g.w, g.scales, g.biases)
+        assert np.array_equal(got[:, E:E + 1], ref), f"{cname} T={T}: shared_expert_gate logit differs"
+
+
 def test_deterministic_and_batch_independent():
     from gpu_util import run_block
     cfg = S.QWEN3_30B_A3B
