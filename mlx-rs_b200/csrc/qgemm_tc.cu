@@ -55,6 +55,10 @@ constexpr int kThreads = kProducers + 64;
 constexpr int kPackSlots = 4;                 // K steps of packed weights in flight
 constexpr int kPackTileBytes = kBM * 32;      // [128 rows][8 words] of one matrix, one K step
 constexpr uint64_t kWaitLimitNs = 200ull * 1000 * 1000;  // bound of one mbarrier wait (200 ms)
+#ifndef MOE_TC_WAIT_SLEEP_NS
+#define MOE_TC_WAIT_SLEEP_NS 2000
+#endif
+constexpr uint32_t kWaitSleepNs = MOE_TC_WAIT_SLEEP_NS;  // suspend hint of one try_wait in a wait loop
 
 // MODE 0: plain, 128 weight rows per CTA; 1: gated (gate and up rows); 2: plain, 256
 // weight rows per CTA as two 128-row accumulators (halves the token-tile reloads).
@@ -91,6 +95,20 @@ MOE_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait that may suspend the thread in hardware for up to `ns` nanoseconds while the
+// phase is incomplete (instead of returning at once), so that waiting warps leave the
+// issue slots to the warps with work
+MOE_DEV bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
 MOE_DEV uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
@@ -100,7 +118,7 @@ MOE_DEV uint64_t global_ns() {
 MOE_DEV bool mbar_wait(uint32_t bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
-  while (!mbar_try_wait(bar, parity))
+  while (!mbar_try_wait_sleep(bar, parity, kWaitSleepNs))
     if (global_ns() - t0 > kWaitLimitNs) return false;
   return true;
 }
@@ -382,15 +400,23 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         }
       }
     };
+    // B tile: 256 rows x 8 chunks of 16 bytes; this thread copies chunks q = p + kProducers i
+    // (rows fixed for the whole K loop, so their source rows and tile offsets are formed once)
+    constexpr int kBChunks = kBN * 8 / kProducers;
+    const uint16_t* bsrc[kBChunks];
+    uint32_t bdst[kBChunks];
+#pragma unroll
+    for (int i = 0; i < kBChunks; ++i) {
+      const int q = p + kProducers * i;
+      const int r = q >> 3, c = q & 7;
+      bdst[i] = sw128_off(r, c);
+      bsrc[i] = r < ntok ? a.x + (size_t)xrow_s[r] * K + (size_t)G0 * kBK + c * 8 : nullptr;
+    }
     auto issue_b = [&](int kk) {
       const uint32_t bt = sbase + (kk % C::kStages) * C::kStageBytes + C::kMats * kATileBytes;
-      // 256 rows x 8 chunks of 16 bytes; this thread: chunks q = p + kProducers i
 #pragma unroll
-      for (int i = 0; i < kBN * 8 / kProducers; ++i) {
-        const int q = p + kProducers * i;
-        const int r = q >> 3, c = q & 7;
-        if (r < ntok) cp_async16(bt + sw128_off(r, c), a.x + (size_t)xrow_s[r] * K + (G0 + kk) * kBK + c * 8);
-      }
+      for (int i = 0; i < kBChunks; ++i)
+        if (bsrc[i]) cp_async16(bt + bdst[i], bsrc[i] + kk * kBK);
       cp_commit();
     };
     constexpr int LA = C::kStages - 1;  // B tiles issued this many stages ahead
