@@ -68,10 +68,18 @@ __global__ void __launch_bounds__(1024) group_small_kernel(GroupArgs a) {
   const int64_t seg = (a.P + 31) / 32;
   const int64_t p0 = warp * seg;
   const int64_t p1 = (p0 + seg < a.P) ? p0 + seg : a.P;
-  for (int64_t p = p0 + lane; p < p1; p += 32) {
-    const uint32_t e = group_key(a, p);
-    if (e < (uint32_t)E) atomicAdd(&wbase[warp * E + e], 1);
+  // the warp's keys stay in registers for the scatter below (P <= 8192: at most 8 rounds
+  // of 32 pairs per warp), all loads issued before the first is used
+  constexpr int kRounds = 8;
+  uint32_t keys[kRounds];
+#pragma unroll
+  for (int r = 0; r < kRounds; ++r) {
+    const int64_t p = p0 + r * 32 + lane;
+    keys[r] = p < p1 ? group_key(a, p) : 0xffffffffu;
   }
+#pragma unroll
+  for (int r = 0; r < kRounds; ++r)
+    if (keys[r] < (uint32_t)E) atomicAdd(&wbase[warp * E + keys[r]], 1);
   __syncthreads();
   // per expert (thread e): prefix over warps; expert totals
   int32_t tot = 0;
@@ -100,10 +108,13 @@ __global__ void __launch_bounds__(1024) group_small_kernel(GroupArgs a) {
   __syncthreads();
   // stable scatter: warp w walks its segment in order, 32 pairs at a time
   int32_t* cur = wbase + warp * E;
-  for (int64_t b = p0; b < p1; b += 32) {
+#pragma unroll
+  for (int r = 0; r < kRounds; ++r) {
+    const int64_t b = p0 + r * 32;
+    if (b >= p1) break;
     const int64_t p = b + lane;
     const bool valid = p < p1;
-    const uint32_t e = valid ? group_key(a, p) : 0xffffffffu;
+    const uint32_t e = keys[r];
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const unsigned lt = (1u << lane) - 1u;
     int32_t pos = 0;
@@ -134,14 +145,16 @@ __global__ void group_hist_kernel(GroupArgs a) {
   for (int e = threadIdx.x; e < a.E; e += blockDim.x) a.hist[(size_t)g * a.E + e] = sh[e];
 }
 
-// One CTA of 1024 threads; thread t owns experts 4t .. 4t+3 (E <= 4096). The [nseg, E]
-// histogram is staged in shared memory (nseg * E * 4 bytes, sized by the caller's
-// choice of segment length), so the per-expert prefix over segments runs at shared
-// memory latency; the results go back to global memory coalesced.
+// One CTA of 1024 threads (E <= 4096). The [nseg, E] histogram is staged in shared memory
+// (nseg * E * 4 bytes, sized by the caller's choice of segment length); the per-expert
+// prefix over segments runs on several threads per expert (runs of segments, then a
+// shuffle scan of the runs' sums), and for the scan over experts thread t owns experts
+// 4t .. 4t+3; the results go back to global memory coalesced.
 __global__ void __launch_bounds__(1024) group_scan_kernel(GroupArgs a) {
   extern __shared__ int32_t hs[];  // [nseg][E]
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t n_act;
+  __shared__ int32_t etot_s[4096];  // per-expert totals (E <= 4096)
   constexpr int EPT = 4;
   const int tid = threadIdx.x;
   const int E = a.E;
@@ -149,21 +162,45 @@ __global__ void __launch_bounds__(1024) group_scan_kernel(GroupArgs a) {
   pdl_wait();
   for (int i = tid; i < n; i += 1024) hs[i] = a.hist[i];
   __syncthreads();
+  // per-expert exclusive prefix over the segments, in place: tpe threads per expert (a
+  // power of two, 1024 / E rounded down, 1 to 32), thread j of an expert owns a run of
+  // consecutive segments; the runs' sums are scanned across the tpe lanes with shuffles
+  int tpe = 1;
+  while (tpe < 32 && tpe * 2 * E <= 1024) tpe *= 2;
+  const int eper = 1024 / tpe;  // experts per pass
+  const int cs = (a.nseg + tpe - 1) / tpe;
+  const int j = tid % tpe;
+  for (int e0 = 0; e0 < E; e0 += eper) {
+    const int e = e0 + tid / tpe;
+    const bool ev = e < E;
+    const int g0 = j * cs, g1 = (g0 + cs < a.nseg) ? g0 + cs : a.nseg;
+    int32_t local = 0;
+    if (ev)
+      for (int g = g0; g < g1; ++g) local += hs[g * E + e];
+    int32_t incl = local;
+    for (int off = 1; off < tpe; off <<= 1) {
+      const int32_t u = __shfl_up_sync(0xffffffffu, incl, off, tpe);
+      if (j >= off) incl += u;
+    }
+    const int32_t etotal = __shfl_sync(0xffffffffu, incl, tpe - 1, tpe);
+    if (ev) {
+      int32_t run = incl - local;
+      for (int g = g0; g < g1; ++g) {
+        const int32_t h = hs[g * E + e];
+        hs[g * E + e] = run;
+        run += h;
+      }
+      if (j == 0) etot_s[e] = etotal;
+    }
+  }
+  __syncthreads();
   int32_t tot[EPT];
   int32_t my_sum = 0, my_act = 0;
 #pragma unroll
   for (int i = 0; i < EPT; ++i) {
     const int e = tid * EPT + i;
-    int32_t run = 0;
-    if (e < E) {
-      for (int g = 0; g < a.nseg; ++g) {
-        const int32_t h = hs[g * E + e];
-        hs[g * E + e] = run;
-        run += h;
-      }
-    }
-    tot[i] = run;
-    my_sum += run;
+    const int32_t run = e < E ? etot_s[e] : 0;
+    tot[i] = run;    my_sum += run;
     my_act += run > 0 ? 1 : 0;
   }
   const int32_t base0 = block_exclusive_scan(my_sum, warp_tot, nullptr);
@@ -217,22 +254,34 @@ __global__ void group_scatter_kernel(GroupArgs a) {
   __syncwarp();
   const int64_t p0 = (int64_t)g * a.seg;
   const int64_t p1 = (p0 + a.seg < a.P) ? p0 + a.seg : a.P;
-  for (int64_t base = p0; base < p1; base += 32) {
-    const int64_t p = base + lane;
-    const bool valid = p < p1;
-    const uint32_t e = valid ? group_key(a, p) : 0xffffffffu;
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    const unsigned lt = (1u << lane) - 1u;
-    int32_t pos = 0;
-    if (valid && e < (uint32_t)a.E) {
-      pos = cur[e] + __popc(peers & lt);
-      a.perm[pos] = (uint32_t)p;
-      if (a.inv) a.inv[p] = (uint32_t)pos;
+  constexpr int kRounds = 8;  // keys of this many rounds of 32 pairs loaded before the first is ranked
+  for (int64_t chunk = p0; chunk < p1; chunk += 32 * kRounds) {
+    uint32_t keys[kRounds];
+#pragma unroll
+    for (int r = 0; r < kRounds; ++r) {
+      const int64_t p = chunk + r * 32 + lane;
+      keys[r] = p < p1 ? group_key(a, p) : 0xffffffffu;
     }
-    __syncwarp();
-    // The highest lane of each group of equal experts advances the cursor.
-    if (valid && e < (uint32_t)a.E && (peers >> lane) == 1u) cur[e] = pos + 1;
-    __syncwarp();
+#pragma unroll
+    for (int r = 0; r < kRounds; ++r) {
+      const int64_t base = chunk + r * 32;
+      if (base >= p1) break;
+      const int64_t p = base + lane;
+      const bool valid = p < p1;
+      const uint32_t e = keys[r];
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      const unsigned lt = (1u << lane) - 1u;
+      int32_t pos = 0;
+      if (valid && e < (uint32_t)a.E) {
+        pos = cur[e] + __popc(peers & lt);
+        a.perm[pos] = (uint32_t)p;
+        if (a.inv) a.inv[p] = (uint32_t)pos;
+      }
+      __syncwarp();
+      // The highest lane of each group of equal experts advances the cursor.
+      if (valid && e < (uint32_t)a.E && (peers >> lane) == 1u) cur[e] = pos + 1;
+      __syncwarp();
+    }
   }
 }
 
@@ -243,7 +292,7 @@ cudaError_t launch_group(const GroupArgs& a, cudaStream_t st) {
     if (err != cudaSuccess) return err;
     return cudaMemsetAsync(a.n_active, 0, sizeof(int32_t), st);
   }
-  if (a.P <= 8192 && a.E <= 512) {
+  if (a.P <= 8192 && a.E <= 512) {  // 8 rounds of 32 pairs per warp of group_small_kernel at most
     const size_t smem = sizeof(int32_t) * 32 * a.E;
     static thread_local int set_dev = -1;
     int dev = 0;
