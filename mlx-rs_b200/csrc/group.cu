@@ -154,13 +154,26 @@ __global__ void __launch_bounds__(1024) group_scan_kernel(GroupArgs a) {
   extern __shared__ int32_t hs[];  // [nseg][E]
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t n_act;
-  __shared__ int32_t etot_s[4096];  // per-expert totals (E <= 4096)
+  __shared__ int32_t etot_s[4096];  // per-expert totals, later per-expert bases (E <= 4096)
   constexpr int EPT = 4;
   const int tid = threadIdx.x;
   const int E = a.E;
   const int n = a.nseg * E;
   pdl_wait();
-  for (int i = tid; i < n; i += 1024) hs[i] = a.hist[i];
+  // 8 loads in flight per thread, then their stores (one CTA moves the whole histogram)
+  for (int i0 = 0; i0 < n; i0 += 8 * 1024) {
+    int32_t v[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int i = i0 + r * 1024 + tid;
+      v[r] = i < n ? __ldcg(a.hist + i) : 0;
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int i = i0 + r * 1024 + tid;
+      if (i < n) hs[i] = v[r];
+    }
+  }
   __syncthreads();
   // per-expert exclusive prefix over the segments, in place: tpe threads per expert (a
   // power of two, 1024 / E rounded down, 1 to 32), thread j of an expert owns a run of
@@ -234,15 +247,15 @@ __global__ void __launch_bounds__(1024) group_scan_kernel(GroupArgs a) {
       tb += nt[i];
     }
   }
-  // segment bases in shared memory -> global, plus the expert's base
+  // segment bases -> global memory, each plus its expert's base (coalesced over the
+  // [nseg, E] layout; the expert bases go through shared memory)
 #pragma unroll
   for (int i = 0; i < EPT; ++i) {
     const int e = tid * EPT + i;
-    if (e < E)
-      for (int g = 0; g < a.nseg; ++g) hs[g * E + e] += ebase[i];
+    if (e < E) etot_s[e] = ebase[i];
   }
   __syncthreads();
-  for (int i = tid; i < n; i += 1024) a.segbase[i] = hs[i];
+  for (int i = tid; i < n; i += 1024) a.segbase[i] = hs[i] + etot_s[i % E];
 }
 
 __global__ void group_scatter_kernel(GroupArgs a) {
