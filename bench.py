@@ -752,22 +752,22 @@ def run_block(args, dev):
 
 
 def ep_stage_times(blk, x, dev, world, reps=6):
-    """Device time of each step of an expert-parallel block (route, the two all-gathers,
-    experts, the all-to-all, finish), from CUDA events between the steps."""
+    """Device time of each step of an expert-parallel block (the all-gather of the token
+    rows, the route of all gathered tokens, experts, the all-to-all, finish), from CUDA
+    events between the steps."""
     import torch
     import torch.distributed as dist
     b = blk.buffers(x.shape[0], dev)
     out = torch.empty_like(x)
-    names = ("route", "all_gather", "experts", "all_to_all", "finish")
+    names = ("all_gather", "route", "experts", "all_to_all", "finish")
     acc = {n: [] for n in names}
     stream = torch.cuda.current_stream(dev)
     for _ in range(reps):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
         ev[0].record(stream)
-        blk.ops.route(blk.bound, x, b.packed)
-        ev[1].record(stream)
         dist.all_gather_into_tensor(b.x_all.view(torch.uint8), x.view(torch.uint8))
-        dist.all_gather_into_tensor(b.packed_all, b.packed)
+        ev[1].record(stream)
+        blk.ops.route(blk.bound, b.x_all, b.packed_all)
         ev[2].record(stream)
         blk.ops.experts(blk.bound, b.x_all, b.packed_all, blk.expert_begin, blk.num_local, b.partial)
         ev[3].record(stream)
@@ -849,7 +849,7 @@ def run_ep_block(args, world, rank, local, dev):
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": workload_config(cfg, regime, T, world, 1),
-        "details": {"experts_per_gpu": n, "collectives": "NCCL all_gather x2 (dispatch), all_to_all (combine)",
+        "details": {"experts_per_gpu": n, "collectives": "NCCL all_gather of the token rows (dispatch; every rank routes all gathered tokens), all_to_all (combine)",
                     "launch": mode,
                     "clock_window": "nvidia-smi every 200 ms across 0.6 s of untimed steps, the timed steps, "
                                     "0.6 s more"},

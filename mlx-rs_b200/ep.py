@@ -5,9 +5,8 @@ qwen3_moe_python_port.rs:420-488). Its experts shard naturally: rank r of `world
 holds the router (replicated) and experts [r*E/world, (r+1)*E/world) of every block,
 and owns T_r tokens of the batch (the same T_r on every rank). One block is
 
-    packed_r  = route(x_r)                          moe_ep_route      [T_r, k] u32
     x_all     = all_gather(x_r)                     NCCL              [world*T_r, H]
-    pk_all    = all_gather(packed_r)                NCCL              [world*T_r, k]
+    pk_all    = route(x_all)                        moe_ep_route      [world*T_r, k] u32
     partial   = experts(x_all, pk_all)              moe_ep_experts    [world*T_r, H] fp32
     received  = all_to_all(partial)                 NCCL, equal parts [world, T_r, H] fp32
     out_r     = finish(received) (+ next RMSNorm)   moe_ep_finish     [T_r, H] bf16
@@ -15,7 +14,10 @@ and owns T_r tokens of the batch (the same T_r on every rank). One block is
 Dispatch is an all-gather rather than a variable all-to-all: with top-8 of 128 experts
 a token reaches 5.3 of 8 ranks on average (1.6 of 2 at world 2), so the gather moves at
 most 1.6x the rows a deduplicated all-to-all would, and it needs no per-step counts on
-the host. Nothing in a block waits for the host, so a whole stack of blocks, the
+the host. Every rank routes every gathered token itself (the router is replicated and
+its logits are bit-exact, so every rank computes the same routing): one router pass over
+world*T_r tokens costs less than a second collective for the routing. Nothing in a block
+waits for the host, so a whole stack of blocks, the
 collectives included, can be captured in one CUDA graph. The combine all-to-all returns
 fp32 partial sums, which the owner adds in rank order; routing is bit-identical to the
 single-device block, outputs differ only by the fp32 association of the k-term sum.
@@ -92,7 +94,6 @@ class _Buffers:
 
     def __init__(self, T: int, H: int, k: int, world: int, device):
         self.T = T
-        self.packed = torch.empty(T, k, dtype=torch.int32, device=device)
         self.x_all = torch.empty(world * T, H, dtype=torch.bfloat16, device=device)
         self.packed_all = torch.empty(world * T, k, dtype=torch.int32, device=device)
         self.partial = torch.empty(world * T, H, dtype=torch.float32, device=device)
@@ -101,7 +102,7 @@ class _Buffers:
     def chunk(self, C: int, c: int, world: int):
         Tc = self.T // C
         H = self.x_all.shape[1]
-        k = self.packed.shape[1]
+        k = self.packed_all.shape[1]
         return (self.x_all.view(C, world * Tc, H)[c], self.packed_all.view(C, world * Tc, k)[c],
                 self.partial.view(C, world * Tc, H)[c], self.received.view(C, world, Tc, H)[c])
 
@@ -156,10 +157,9 @@ class ExpertParallelBlock:
         C = self.chunks if self.chunks is not None else default_chunks(T)
         if C < 1 or T % C:
             raise MlxError("moe_ep_route", 1, f"{T} tokens do not split into {C} chunks")
-        self.ops.route(self.bound, x, b.packed)
         if C == 1:
             dist.all_gather_into_tensor(b.x_all.view(torch.uint8), x.view(torch.uint8), group=g)
-            dist.all_gather_into_tensor(b.packed_all, b.packed, group=g)
+            self.ops.route(self.bound, b.x_all, b.packed_all)
             self.ops.experts(self.bound, b.x_all, b.packed_all, self.expert_begin, self.num_local, b.partial)
             dist.all_to_all_single(b.received.view(-1), b.partial.view(-1), group=g)
             self.ops.finish(b.received, self.world, out, norm_weight, eps, normed)
@@ -170,10 +170,9 @@ class ExpertParallelBlock:
         rows = [slice(c * Tc, (c + 1) * Tc) for c in range(C)]
 
         def gather(c):
-            xa, pa, _, _ = b.chunk(C, c, self.world)
+            xa, _, _, _ = b.chunk(C, c, self.world)
             return (dist.all_gather_into_tensor(xa.view(torch.uint8), x[rows[c]].view(torch.uint8), group=g,
-                                                async_op=True),
-                    dist.all_gather_into_tensor(pa, b.packed[rows[c]], group=g, async_op=True))
+                                                async_op=True),)
 
         pending = gather(0)
         combines = []
@@ -183,6 +182,7 @@ class ExpertParallelBlock:
             if c + 1 < C:
                 pending = gather(c + 1)
             xa, pa, part, recv = b.chunk(C, c, self.world)
+            self.ops.route(self.bound, xa, pa)
             self.ops.experts(self.bound, xa, pa, self.expert_begin, self.num_local, part)
             combines.append(dist.all_to_all_single(recv.view(-1), part.view(-1), group=g, async_op=True))
         for c in range(C):

@@ -52,8 +52,13 @@ def _worker(rank, world, port, case, q):
             out = blk.forward(xr)
             ref, idx, w = O.block_forward(bw, x)
             rows = slice(rank * T_r, (rank + 1) * T_r)
-            pk = blk.buffers(T_r, xr.device).packed.numpy().view(np.uint32)
-            assert np.array_equal(pk, O.pack_routing(idx, w)[rows]), "routing differs"
+            # every rank routes every gathered token: its packed routing covers all ranks'
+            # rows, in the gathered order (with C chunks: chunk-major, then rank, then row)
+            pk = blk.buffers(T_r, xr.device).packed_all.numpy().view(np.uint32)
+            C = 3 if case == "chunked" else 1
+            Tc = T_r // C
+            order = [r * T_r + c * Tc + i for c in range(C) for r in range(world) for i in range(Tc)]
+            assert np.array_equal(pk, O.pack_routing(idx, w)[order]), "routing differs"
             m = assert_close(bits(out), ref[rows], f"ep rank {rank}")
             res = {"frac_exact": m["frac_exact"]}
         elif case == "stack":
