@@ -514,6 +514,12 @@ bool use_tc(int64_t rows, int64_t experts, int N, int K) {
 // decode went from 0.265 to 0.300 ms per step.) MOE_B200_TC=0 puts every expert on the
 // GEMV, =1 every expert on tcgen05.
 constexpr int kTcMinRows = 32;
+// Expected rows per expert from which every expert runs on tcgen05. Measured on the B200
+// (CUDA-graph blocks, L2 flushed), against the previous 128: Qwen1.5-MoE T=512 (34 rows
+// per expert) 400 -> 356 us, Qwen3-30B-A3B T=384 (24) 375 -> 331 us and T=512 (32) 371
+// -> 342 us, LFM2-8B-A1B T=256 (32) 161 -> 129 us; at 16 rows per expert the GEMV, the
+// hybrid and all-tcgen05 are level (Qwen3 T=256: 338 us).
+constexpr int kTcAllRows = 24;
 struct ExpertPlan {
   bool tc_gu = false, tc_dn = false;      // launch the tcgen05 kernel
   bool gemv_gu = true, gemv_dn = true;    // launch the GEMV
@@ -532,8 +538,9 @@ ExpertPlan plan_experts(int64_t P, int E, int I, int H) {
     p.tc_dn = shape_dn;
     p.gemv_gu = !shape_gu;
     p.gemv_dn = !shape_dn;
-  } else if (P >= (int64_t)4 * kTcMinRows * E) {
-    // prefill: nearly every expert is large, all go to tcgen05 (no GEMV launch)
+  } else if (P >= (int64_t)kTcAllRows * E) {
+    // prefill, and expert-parallel decode at 8 GPUs: most experts are large, all go to
+    // tcgen05 (no GEMV launch)
     p.tc_gu = shape_gu;
     p.tc_dn = shape_dn;
     p.gemv_gu = !shape_gu;
