@@ -69,6 +69,8 @@ def parse():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--ep-partials", choices=("f32", "bf16"), default="f32",
+                    help="expert-parallel combine: fp32 partial sums (default) or bf16 (half the bytes)")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the per-configuration sub-records of the default run")
     return ap.parse_args()
@@ -799,7 +801,8 @@ def run_ep_block(args, world, rank, local, dev):
     cfg, bw_host, T, regime, _ = make_workload(args, S)
     H = cfg.hidden
     e0, n = expert_range(cfg.num_experts, world, rank)
-    blk = ExpertParallelBlock(local_weights(S.to_device(bw_host, dev), e0, n), cfg, expert_begin=e0, num_local=n)
+    blk = ExpertParallelBlock(local_weights(S.to_device(bw_host, dev), e0, n), cfg, expert_begin=e0, num_local=n,
+                              partials=args.ep_partials)
     del bw_host
     pool = 8
     xs_host = [S.host_x(1000 + 97 * rank + i, T, H) for i in range(pool)]
@@ -849,7 +852,7 @@ def run_ep_block(args, world, rank, local, dev):
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": workload_config(cfg, regime, T, world, 1),
-        "details": {"experts_per_gpu": n, "collectives": "NCCL all_gather of the token rows (dispatch; every rank routes all gathered tokens), all_to_all (combine)",
+        "details": {"experts_per_gpu": n, "collectives": "NCCL all_gather of the token rows (dispatch; every rank routes all gathered tokens), all_to_all (combine)", "ep_partials": args.ep_partials,
                     "launch": mode,
                     "clock_window": "nvidia-smi every 200 ms across 0.6 s of untimed steps, the timed steps, "
                                     "0.6 s more"},
@@ -885,7 +888,8 @@ def run_stack(args, world, rank, local, dev):
     for l in range(layers):
         bw = S.device_block(cfg, seed * 1000 + l, dev)  # identical on every rank
         if world > 1:
-            blocks.append(ExpertParallelBlock(local_weights(bw, e0, n), cfg, expert_begin=e0, num_local=n))
+            blocks.append(ExpertParallelBlock(local_weights(bw, e0, n), cfg, expert_begin=e0, num_local=n,
+                                              partials=args.ep_partials))
         else:
             blocks.append(SparseMoeBlock(bw, cfg))
         del bw

@@ -280,6 +280,21 @@ int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_we
                    const void* x_all, int64_t T_all, const uint32_t* packed_all,
                    int32_t expert_begin, int32_t num_local, float* partial);
 
+/* moe_ep_experts with each partial sum rounded once to bf16 (round to nearest even) into
+ * partial [T_all, hidden] bf16: half the bytes through the combine's all-to-all. The
+ * owner's sum (moe_ep_finish_bf16) then adds bf16-rounded partials, which differs from
+ * the fp32 form only for tokens whose experts lie on more than one rank, but there
+ * partials of opposite sign that nearly cancel lose relative accuracy (the fp32 form is
+ * the one held to the block's parity bound). */
+int moe_ep_experts_bf16(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts,
+                        const void* x_all, int64_t T_all, const uint32_t* packed_all,
+                        int32_t expert_begin, int32_t num_local, void* partial);
+
+/* moe_ep_finish over bf16 partials [world, rows, hidden] (widened exactly, summed in fp32
+ * in rank order). */
+int moe_ep_finish_bf16(moe_ctx* ctx, const void* partials, int32_t world, int64_t rows,
+                       int64_t hidden, void* out, const void* norm_weight, float eps, void* normed);
+
 /* out[r] = bf16(sum over s = 0..world-1 in order of partials[s, r, :]) for r < rows
  * (partials [world, rows, hidden] fp32, the all-to-all's output). With norm_weight
  * (and normed), also normed[r] = moe_fast_rms_norm(out[r], norm_weight, eps): the

@@ -102,6 +102,11 @@ SIGNATURES = {
                                  C.c_void_p]),
     "moe_ep_finish": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int64, C.c_int64,
                                 C.c_void_p, C.c_void_p, C.c_float, C.c_void_p]),
+    "moe_ep_experts_bf16": (C.c_int, [C.c_void_p, C.POINTER(BlockConfig), C.POINTER(BlockWeights),
+                                      C.c_void_p, C.c_int64, C.c_void_p, C.c_int32, C.c_int32,
+                                      C.c_void_p]),
+    "moe_ep_finish_bf16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int64, C.c_int64,
+                                     C.c_void_p, C.c_void_p, C.c_float, C.c_void_p]),
 }
 
 

@@ -1237,12 +1237,14 @@ int moe_ep_route(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weig
   return run_route(ctx, cfg, wts, x, T, carve_route(ctx->scratch, cfg, T), nullptr, packed);
 }
 
-int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x_all,
-                   int64_t T_all, const uint32_t* packed_all, int32_t expert_begin, int32_t num_local,
-                   float* partial) {
+namespace {
+// moe_ep_experts / moe_ep_experts_bf16: partial sums into partial (fp32) or partial_bf16.
+int ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x_all,
+               int64_t T_all, const uint32_t* packed_all, int32_t expert_begin, int32_t num_local, float* partial_f32,
+               uint16_t* partial_bf16, const char* fn) {
+  void* partial = partial_f32 ? static_cast<void*>(partial_f32) : static_cast<void*>(partial_bf16);
   if (!ctx) return MOE_ERR_INVALID;
   ctx->last_error.clear();
-  const char* fn = "moe_ep_experts";
   int rc = check_experts(ctx, cfg, wts, fn);
   if (rc) return rc;
   if (num_local <= 0 || expert_begin < 0 || (int64_t)expert_begin + num_local > cfg->num_experts)
@@ -1337,16 +1339,32 @@ int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_we
   pa.T = (int)T_all;
   pa.k = k;
   pa.H = H;
-  pa.partial = partial;
+  pa.partial = partial_f32;
+  pa.partial_bf16 = partial_bf16;
   MOE_CUDA(ctx, moe::launch_ep_partial(pa, ctx->stream));
   return MOE_OK;
 }
+}  // namespace
 
-int moe_ep_finish(moe_ctx* ctx, const float* partials, int32_t world, int64_t rows, int64_t hidden, void* out,
-                  const void* norm_weight, float eps, void* normed) {
+int moe_ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x_all,
+                   int64_t T_all, const uint32_t* packed_all, int32_t expert_begin, int32_t num_local,
+                   float* partial) {
+  return ep_experts(ctx, cfg, wts, x_all, T_all, packed_all, expert_begin, num_local, partial, nullptr,
+                    "moe_ep_experts");
+}
+
+int moe_ep_experts_bf16(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x_all,
+                        int64_t T_all, const uint32_t* packed_all, int32_t expert_begin, int32_t num_local,
+                        void* partial) {
+  return ep_experts(ctx, cfg, wts, x_all, T_all, packed_all, expert_begin, num_local, nullptr,
+                    static_cast<uint16_t*>(partial), "moe_ep_experts_bf16");
+}
+
+namespace {
+int ep_finish(moe_ctx* ctx, const void* partials, bool bf16, int32_t world, int64_t rows, int64_t hidden, void* out,
+              const void* norm_weight, float eps, void* normed, const char* fn) {
   if (!ctx) return MOE_ERR_INVALID;
   ctx->last_error.clear();
-  const char* fn = "moe_ep_finish";
   if (world <= 0 || rows < 0 || hidden <= 0 || hidden % 8 != 0 || hidden > INT32_MAX)
     return fail(ctx, MOE_ERR_INVALID, "%s: bad world/rows/hidden (hidden a positive multiple of 8)", fn);
   if (rows == 0) return MOE_OK;
@@ -1358,10 +1376,26 @@ int moe_ep_finish(moe_ctx* ctx, const float* partials, int32_t world, int64_t ro
     return fail(ctx, MOE_ERR_INVALID, "%s: norm_weight and normed must be 16-byte aligned", fn);
   DeviceGuard g(ctx->device);
   if (!g.ok) return fail(ctx, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", ctx->device);
-  MOE_CUDA(ctx, moe::launch_ep_finish(partials, world, rows, (int)hidden, static_cast<uint16_t*>(out),
-                                      static_cast<const uint16_t*>(norm_weight), eps,
-                                      static_cast<uint16_t*>(normed), ctx->stream));
+  if (bf16)
+    MOE_CUDA(ctx, moe::launch_ep_finish_bf16(static_cast<const uint16_t*>(partials), world, rows, (int)hidden,
+                                             static_cast<uint16_t*>(out), static_cast<const uint16_t*>(norm_weight),
+                                             eps, static_cast<uint16_t*>(normed), ctx->stream));
+  else
+    MOE_CUDA(ctx, moe::launch_ep_finish(static_cast<const float*>(partials), world, rows, (int)hidden,
+                                        static_cast<uint16_t*>(out), static_cast<const uint16_t*>(norm_weight), eps,
+                                        static_cast<uint16_t*>(normed), ctx->stream));
   return MOE_OK;
+}
+}  // namespace
+
+int moe_ep_finish(moe_ctx* ctx, const float* partials, int32_t world, int64_t rows, int64_t hidden, void* out,
+                  const void* norm_weight, float eps, void* normed) {
+  return ep_finish(ctx, partials, false, world, rows, hidden, out, norm_weight, eps, normed, "moe_ep_finish");
+}
+
+int moe_ep_finish_bf16(moe_ctx* ctx, const void* partials, int32_t world, int64_t rows, int64_t hidden, void* out,
+                       const void* norm_weight, float eps, void* normed) {
+  return ep_finish(ctx, partials, true, world, rows, hidden, out, norm_weight, eps, normed, "moe_ep_finish_bf16");
 }
 
 int moe_ctx_status(moe_ctx* ctx, int32_t* status) {

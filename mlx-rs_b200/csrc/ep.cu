@@ -1,17 +1,20 @@
 // ep.cu — the two kernels that expert parallelism adds around the block's kernels.
 //
 // Under expert parallelism rank r owns experts [e0, e0 + E_l) of every block and the
-// tokens [r*T_l, (r+1)*T_l). Each rank routes its own tokens, the token rows and their
-// packed routing (expert | bf16 weight << 16) are all-gathered, every rank runs its
-// experts over the pairs that selected them, and the per-token partial sums travel back
+// tokens [r*T_l, (r+1)*T_l). The token rows are all-gathered, every rank routes all of
+// them (packed routing: expert | bf16 weight << 16), runs its experts over the pairs that
+// selected them, and the per-token partial sums travel back
 // to the token's owner with an all-to-all, where they are added in rank order.
 //
 // ep_partial: the combine of SparseMoeBlock::forward (expert_out * score, sum_axis(1),
 //   qwen3_moe_python_port.rs:471-472; lfm2_moe_python_port.rs:718-732) restricted to
 //   the local experts: partial[t] = sum over j = 0..k-1 in index order, of the local
-//   pairs only, of bf16(y * w_j), in fp32 and not rounded (the owner rounds once).
+//   pairs only, of bf16(y * w_j), in fp32 and not rounded (the owner rounds once), or
+//   rounded once to bf16 (half the bytes through the combine's all-to-all; the owner's
+//   sum then adds bf16-rounded partials).
 //   Each thread owns 8 consecutive hidden elements of one token, as in combine.cu.
-// ep_finish: out[t] = bf16(sum over ranks s in order of partial_s[t]); optionally the
+// ep_finish: out[t] = bf16(sum over ranks s in order of partial_s[t]) (fp32 or bf16
+//   partials, summed in fp32); optionally the
 //   next block's RMSNorm (RmsNorm::forward, crates/mlx-nn/src/rms_norm.rs:30-34) of
 //   out in the same pass, with the canonical sum of squares of rms_norm_kernel.
 #include "common.cuh"
@@ -61,13 +64,36 @@ __global__ void __launch_bounds__(256) ep_partial_kernel(EpPartialArgs a) {
       }
     }
   }
+  if (a.partial_bf16) {
+    uint4 o;
+    o.x = (uint32_t)f2bf(acc[0]) | ((uint32_t)f2bf(acc[1]) << 16);
+    o.y = (uint32_t)f2bf(acc[2]) | ((uint32_t)f2bf(acc[3]) << 16);
+    o.z = (uint32_t)f2bf(acc[4]) | ((uint32_t)f2bf(acc[5]) << 16);
+    o.w = (uint32_t)f2bf(acc[6]) | ((uint32_t)f2bf(acc[7]) << 16);
+    *reinterpret_cast<uint4*>(a.partial_bf16 + (size_t)t * a.H + h) = o;
+    return;
+  }
   float4* dst = reinterpret_cast<float4*>(a.partial + (size_t)t * a.H + h);
   dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
   dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
 }
 
-// One warp per row; lane l owns the chunks of 8 elements c = l, l + 32, ...
-__global__ void __launch_bounds__(256) ep_finish_kernel(const float* __restrict__ recv, int world, int64_t rows,
+// 8 consecutive partial values of one rank as fp32 (bf16 partials widen exactly).
+MOE_DEV void load8(const float* p, float (&v)[8]) {
+  const float4 x0 = reinterpret_cast<const float4*>(p)[0], x1 = reinterpret_cast<const float4*>(p)[1];
+  v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+  v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+}
+MOE_DEV void load8(const uint16_t* p, float (&v)[8]) {
+  const uint4 x = *reinterpret_cast<const uint4*>(p);
+  v[0] = bf_lo(x.x); v[1] = bf_hi(x.x); v[2] = bf_lo(x.y); v[3] = bf_hi(x.y);
+  v[4] = bf_lo(x.z); v[5] = bf_hi(x.z); v[6] = bf_lo(x.w); v[7] = bf_hi(x.w);
+}
+
+// One warp per row; lane l owns the chunks of 8 elements c = l, l + 32, ... Partials in
+// fp32 or bf16 (PT).
+template <class PT>
+__global__ void __launch_bounds__(256) ep_finish_kernel(const PT* __restrict__ recv, int world, int64_t rows,
                                                         int H, uint16_t* __restrict__ out,
                                                         const uint16_t* __restrict__ norm_w, float eps,
                                                         uint16_t* __restrict__ normed) {
@@ -84,16 +110,10 @@ __global__ void __launch_bounds__(256) ep_finish_kernel(const float* __restrict_
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = 0.0f;
     for (int s = 0; s < world; ++s) {
-      const float4* src = reinterpret_cast<const float4*>(recv + s * rank_stride + (size_t)r * H + c * 8);
-      const float4 x0 = src[0], x1 = src[1];
-      v[0] = __fadd_rn(v[0], x0.x);
-      v[1] = __fadd_rn(v[1], x0.y);
-      v[2] = __fadd_rn(v[2], x0.z);
-      v[3] = __fadd_rn(v[3], x0.w);
-      v[4] = __fadd_rn(v[4], x1.x);
-      v[5] = __fadd_rn(v[5], x1.y);
-      v[6] = __fadd_rn(v[6], x1.z);
-      v[7] = __fadd_rn(v[7], x1.w);
+      float x[8];
+      load8(recv + s * rank_stride + (size_t)r * H + c * 8, x);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = __fadd_rn(v[i], x[i]);
     }
     uint16_t o[8];
 #pragma unroll
@@ -139,8 +159,15 @@ cudaError_t launch_ep_partial(const EpPartialArgs& a, cudaStream_t st) {
 cudaError_t launch_ep_finish(const float* recv, int world, int64_t rows, int H, uint16_t* out,
                              const uint16_t* norm_w, float eps, uint16_t* normed, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
-  return launch_k(ep_finish_kernel, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0, st, recv, world, rows, H, out,
-                  norm_w, eps, normed);
+  return launch_k(ep_finish_kernel<float>, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0, st, recv, world, rows, H,
+                  out, norm_w, eps, normed);
+}
+
+cudaError_t launch_ep_finish_bf16(const uint16_t* recv, int world, int64_t rows, int H, uint16_t* out,
+                                  const uint16_t* norm_w, float eps, uint16_t* normed, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  return launch_k(ep_finish_kernel<uint16_t>, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0, st, recv, world, rows,
+                  H, out, norm_w, eps, normed);
 }
 
 }  // namespace moe

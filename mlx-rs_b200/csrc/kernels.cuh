@@ -241,13 +241,17 @@ struct EpPartialArgs {
   const uint32_t* packed;   // [T, k] expert | bf16(weight) << 16
   uint32_t e0;
   int E_l, T, k, H;
-  float* partial;           // [T, H]
+  float* partial;           // [T, H] fp32, or null when partial_bf16 is given
+  uint16_t* partial_bf16;   // [T, H] bf16 (round to nearest even), or null
 };
 cudaError_t launch_ep_partial(const EpPartialArgs& a, cudaStream_t st);
 // out[r] = bf16(sum over ranks s = 0..world-1 in order of recv[s, r, :]) for r < rows;
 // with norm_w, also normed[r] = RMSNorm(out[r]) * norm_w as launch_rms_norm computes it.
 cudaError_t launch_ep_finish(const float* recv, int world, int64_t rows, int H, uint16_t* out,
                              const uint16_t* norm_w, float eps, uint16_t* normed, cudaStream_t st);
+// The same over bf16 partials (each widened to fp32 exactly, then summed in rank order).
+cudaError_t launch_ep_finish_bf16(const uint16_t* recv, int world, int64_t rows, int H, uint16_t* out,
+                                  const uint16_t* norm_w, float eps, uint16_t* normed, cudaStream_t st);
 cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, float eps, int64_t rows, int dim,
                             uint16_t* out, cudaStream_t st);
 // The Gemma4 router's input: out[r] (f32) = f32(RMSNorm(x[r]) with unit weight, rounded to

@@ -37,11 +37,14 @@ class OracleEpOps:
     def experts(self, blk, x_all, packed_all, expert_begin, num_local, partial):
         p = O.ep_partials(blk, bits(x_all), packed_all.numpy().view(np.uint32), expert_begin, num_local,
                           nthreads=1)
-        partial.copy_(torch.from_numpy(p))
+        if partial.dtype == torch.bfloat16:  # the partial sums rounded once (to nearest even)
+            partial.copy_(from_bits(S.f32_to_bf16_bits(p)))
+        else:
+            partial.copy_(torch.from_numpy(p))
 
     def finish(self, received, world, out, norm_weight=None, eps=1e-6, normed=None):
         nw = None if norm_weight is None else bits(norm_weight)
-        o, n = O.ep_finish(received.numpy(), nw, eps)
+        o, n = O.ep_finish(received.float().numpy(), nw, eps)  # bf16 partials widen exactly
         out.copy_(from_bits(o))
         if normed is not None:
             normed.copy_(from_bits(n))

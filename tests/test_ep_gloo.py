@@ -40,14 +40,15 @@ def _worker(rank, world, port, case, q):
         from parity import assert_close
 
         res = {}
-        if case in ("block", "sigmoid", "chunked"):
+        if case in ("block", "block_bf16", "sigmoid", "chunked"):
             cfg = CFG if case != "sigmoid" else CFG_SIG
             bw = S.host_block(cfg, 41)
             T_r = 6 if case == "chunked" else 5
             x = S.host_x(41, world * T_r, cfg.hidden)
             e0, n = expert_range(cfg.num_experts, world, rank)
             blk = ExpertParallelBlock(local_block(bw, e0, n), cfg, expert_begin=e0, num_local=n, ops=OracleEpOps(),
-                                      chunks=3 if case == "chunked" else None)
+                                      chunks=3 if case == "chunked" else None,
+                                      partials="bf16" if case == "block_bf16" else "f32")
             xr = from_bits(x[rank * T_r:(rank + 1) * T_r])
             out = blk.forward(xr)
             ref, idx, w = O.block_forward(bw, x)
@@ -109,8 +110,16 @@ def _run(case, world=2):
 
 @pytest.mark.parametrize("world", [2, 4])
 def test_ep_block_matches_single_device_oracle(world):
+    """fp32 partial sums (the default): the single-device result up to the fp32
+    association of the k-term sum, so nearly every element is bit-identical."""
     r = _run("block", world)
     assert all(p[1]["frac_exact"] > 0.99 for p in r.values()), r
+
+
+def test_ep_block_bf16_partials_world2():
+    """bf16 partial sums (partials="bf16"): within the parity tolerance of the
+    single-device block (checked in every rank)."""
+    _run("block_bf16", 2)
 
 
 def test_ep_sigmoid_routing_world2():

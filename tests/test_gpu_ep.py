@@ -20,7 +20,7 @@ from parity import ULP_TOL, ULP_TOL_TC, assert_close
 pytestmark = pytest.mark.gpu
 
 
-def _emulate(cfg, seed, T_r, world, x_seed, norm=False):
+def _emulate(cfg, seed, T_r, world, x_seed, norm=False, partial_dtype=None):
     import torch
     from gpu_util import dev_bits, make_block, to_dev
     from mlx_rs_b200.ep import CudaEpOps, expert_range, local_weights
@@ -38,7 +38,7 @@ def _emulate(cfg, seed, T_r, world, x_seed, norm=False):
         ops.route(bound[r], x_all[r * T_r:(r + 1) * T_r].contiguous(), packed[r * T_r:(r + 1) * T_r])
     partials = []
     for r, (e0, n) in enumerate(shares):
-        p = torch.empty(world * T_r, H, dtype=torch.float32, device="cuda")
+        p = torch.empty(world * T_r, H, dtype=partial_dtype or torch.float32, device="cuda")
         ops.experts(bound[r], x_all, packed, e0, n, p)
         partials.append(p)
     out = torch.empty(world * T_r, H, dtype=torch.bfloat16, device="cuda")
@@ -70,6 +70,20 @@ def test_ep_decode_qwen3_matches_block_and_oracle(world):
     assert m["frac_exact"] > 0.99, m
     y, _, _ = O.block_forward(bw, x)
     assert_close(out, y, f"EP world {world} vs oracle", ULP_TOL)
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_ep_bf16_partials_qwen3(world):
+    """bf16 partial sums through the combine (moe_ep_experts_bf16 / moe_ep_finish_bf16):
+    within the tolerance of the single-device block and of the oracle; a token whose
+    experts all lie on one rank gets that rank's sum rounded once, as the block does."""
+    import oracle as O
+    import torch
+    cfg = S.QWEN3_30B_A3B
+    bw, x, out, ref = _emulate(cfg, 1, 8, world, 320 + world, partial_dtype=torch.bfloat16)
+    assert_close(out, ref, f"EP bf16 partials world {world} vs block", ULP_TOL)
+    y, _, _ = O.block_forward(bw, x)
+    assert_close(out, y, f"EP bf16 partials world {world} vs oracle", ULP_TOL)
 
 
 def test_ep_lfm2_sigmoid_world2():
