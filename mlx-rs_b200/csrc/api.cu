@@ -528,7 +528,10 @@ struct ExpertPlan {
   int max_tiles = 0;                      // tcgen05 grid.y
 };
 
-ExpertPlan plan_experts(int64_t P, int E, int I, int H) {
+// max_rows: the most rows one expert can receive (the block: T, since a token selects an
+// expert at most once; gather_qmm: every row). Below kTcMinRows no expert can reach the
+// tcgen05 threshold and its launches (whose CTAs would all leave at once) are skipped.
+ExpertPlan plan_experts(int64_t P, int E, int I, int H, int64_t max_rows) {
   ExpertPlan p;
   const bool shape_gu = I % 128 == 0 && H % 64 == 0, shape_dn = H % 128 == 0 && I % 64 == 0;
   const char* v = std::getenv("MOE_B200_TC");
@@ -538,6 +541,8 @@ ExpertPlan plan_experts(int64_t P, int E, int I, int H) {
     p.tc_dn = shape_dn;
     p.gemv_gu = !shape_gu;
     p.gemv_dn = !shape_dn;
+  } else if (max_rows < kTcMinRows) {
+    return p;  // GEMV only
   } else if (P >= (int64_t)kTcAllRows * E) {
     // prefill, and expert-parallel decode at 8 GPUs: most experts are large, all go to
     // tcgen05 (no GEMV launch)
@@ -567,7 +572,7 @@ ExpertPlan plan_experts(int64_t P, int E, int I, int H) {
 // moe_gather_qmm and moe_gather_qmm_noalloc, which differ only in where the scratch lives.
 cudaError_t moe::launch_gather_qmm(const moe::GatherCall& c, cudaStream_t st) {
   // one matrix: the gate/up fields of the plan with I = N, H = K
-  const ExpertPlan plan = plan_experts(c.batch, c.E, c.N, c.K);
+  const ExpertPlan plan = plan_experts(c.batch, c.E, c.N, c.K, c.batch);
   moe::GroupArgs ga = c.g;
   ga.key = c.rhs;
   ga.key_packed = 0;
@@ -756,7 +761,7 @@ int run_block(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights
     return MOE_OK;
   }
   ctx->last_block_fused = false;
-  const ExpertPlan plan = plan_experts(P, E, I, H);
+  const ExpertPlan plan = plan_experts(P, E, I, H, T);
   rc = run_route(ctx, cfg, wts, x, T, ws, ev, nullptr, plan.min_rows);
   if (rc) return rc;
 
@@ -1114,7 +1119,7 @@ int moe_gemma4_block_forward(moe_ctx* ctx, const moe_block_config* cfg, const mo
   ta.idx = ws.idx;
   ta.weights = nullptr;
   MOE_CUDA(ctx, moe::launch_topk(ta, ctx->stream));
-  const ExpertPlan plan = plan_experts(P, E, c.moe_inter, H);
+  const ExpertPlan plan = plan_experts(P, E, c.moe_inter, H, T);
   moe::GroupArgs ga{};
   ga.key = ws.idx;
   ga.P = P;
@@ -1280,7 +1285,7 @@ int ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weight
   // Path choice per expert as in moe_block_forward, on the expected rows per expert of
   // all pairs over all E experts; the grids cover every local pair in the worst case
   // and idle CTAs leave at once.
-  ExpertPlan plan = plan_experts(P, E, I, H);
+  ExpertPlan plan = plan_experts(P, E, I, H, T_all);
   plan.max_tiles = (int)(P / moe::kTcTileRows +
                          std::min<int64_t>(El, plan.min_rows ? P / plan.min_rows : P) + 1);
   ga.tile_start = ws.tile_start;
