@@ -408,12 +408,37 @@ static float sum_canonical(const float* v, int64_t n) {
     return butterfly32(acc);
 }
 
-/* softmax over the last axis of bf16 rows, fp32 internally (mlx_softmax_axis with
- * precise=false, crates/mlx-core/src/ops.rs:226-233): m = max, e_i = exp(l_i - m),
- * p_i = bf16(e_i / canonical_sum(e)). */
+/* Internal precision of the routing softmax. The reference calls mlx_softmax_axis with
+ * precise=false (crates/mlx-core/src/ops.rs:226-233) on bf16 logits; whether MLX then
+ * computes in fp32 or in the input type depends on its backend and version, neither of
+ * which is visible here, so the oracle offers both:
+ *   ORACLE_SOFTMAX_F32 (default, and what the CUDA path computes): m = max,
+ *     e_i = exp(l_i - m) in fp32, p_i = bf16(e_i / canonical_sum(e));
+ *   ORACLE_SOFTMAX_BF16: every intermediate in bf16, the accumulation type being the
+ *     input type: d_i = bf16(l_i - m), e_i = bf16(exp(d_i)), s = bf16(s + e_i) in element
+ *     order, r = bf16(1 / s), p_i = bf16(e_i * r). */
+static int g_softmax_mode = ORACLE_SOFTMAX_F32;
+
+int oracle_set_softmax_precision(int mode) {
+    if (mode != ORACLE_SOFTMAX_F32 && mode != ORACLE_SOFTMAX_BF16) return -1;
+    const int prev = g_softmax_mode;
+    g_softmax_mode = mode;
+    return prev;
+}
+
 static void softmax_row_f(const float* l, int64_t n, float* ex, uint16_t* p) {
     float m = -INFINITY;
     for (int64_t i = 0; i < n; ++i) m = l[i] > m ? l[i] : m;
+    if (g_softmax_mode == ORACLE_SOFTMAX_BF16) {
+        float s = 0.0f;
+        for (int64_t i = 0; i < n; ++i) {
+            ex[i] = rbf(oracle_exp(rbf(l[i] - m)));
+            s = rbf(s + ex[i]);
+        }
+        const float r = rbf(1.0f / s);
+        for (int64_t i = 0; i < n; ++i) p[i] = f2bf(ex[i] * r);
+        return;
+    }
     for (int64_t i = 0; i < n; ++i) ex[i] = oracle_exp(l[i] - m);
     const float s = sum_canonical(ex, n);
     for (int64_t i = 0; i < n; ++i) p[i] = f2bf(ex[i] / s);

@@ -18,6 +18,8 @@
  *     oracle_dot_canonical();
  *   - affine dequantisation: w = fmaf(scale, q, bias) in fp32;
  *   - softmax: fp32 internally (max, exp, canonical sum, divide), bf16 result;
+ *     oracle_set_softmax_precision(ORACLE_SOFTMAX_BF16) switches the routing softmax
+ *     to bf16 intermediates (MLX's precise=false may compute in the input type);
  *   - exp: oracle_exp(), Cody-Waite range reduction + degree-7 Taylor polynomial;
  *   - argpartition ties: (value desc, index asc), the rule the reference's own
  *     host validator uses (qwen3_moe_python_port.rs:89-93, 491-510);
@@ -75,6 +77,12 @@ typedef struct {
 } oracle_block_weights;
 
 float oracle_exp(float x);
+
+/* Internal precision of the routing softmax (process-wide; returns the previous mode, or
+ * -1 for an unknown mode). ORACLE_SOFTMAX_F32 is the default. */
+#define ORACLE_SOFTMAX_F32 0
+#define ORACLE_SOFTMAX_BF16 1
+int oracle_set_softmax_precision(int mode);
 float oracle_sigmoid(float x);
 uint16_t oracle_f32_to_bf16(float x);
 

@@ -54,6 +54,8 @@ def lib():
                 os.path.exists(src) and os.path.getmtime(_LIB_PATH) < os.path.getmtime(src)):
             build()
         L = C.CDLL(_LIB_PATH)
+        L.oracle_set_softmax_precision.restype = C.c_int
+        L.oracle_set_softmax_precision.argtypes = [C.c_int]
         L.oracle_exp.restype = C.c_float
         L.oracle_exp.argtypes = [C.c_float]
         L.oracle_sigmoid.restype = C.c_float
@@ -102,6 +104,23 @@ def _check(rc, name):
 
 def exp(x: float) -> float:
     return lib().oracle_exp(x)
+
+
+class softmax_precision:
+    """Context manager: the routing softmax computes with "f32" (default) or "bf16"
+    intermediates (see moe_oracle.c, oracle_set_softmax_precision)."""
+
+    def __init__(self, mode: str):
+        if mode not in ("f32", "bf16"):
+            raise ValueError(mode)
+        self.mode = 0 if mode == "f32" else 1
+
+    def __enter__(self):
+        self.prev = lib().oracle_set_softmax_precision(self.mode)
+        return self
+
+    def __exit__(self, *exc):
+        lib().oracle_set_softmax_precision(self.prev)
 
 
 def sigmoid(x: float) -> float:

@@ -213,3 +213,39 @@ def test_gemma4_oracle_vs_numpy_restatement():
     np.testing.assert_allclose(w, wr, rtol=1e-5)
     rel = np.abs(y - yr).mean() / np.abs(yr).mean()
     assert rel < 2e-6, rel
+
+
+def test_softmax_precision_switch():
+    """The routing softmax's internal precision is a switch: f32 (default, what the CUDA
+    path computes) or bf16 intermediates, for a reference whose precise=false softmax
+    computes in the input type. bf16 mode against a restatement in Python: d = bf16(l - m),
+    e = bf16(exp(d)), s = bf16(s + e) in element order, p = bf16(e * bf16(1 / s))."""
+    rng = np.random.default_rng(5)
+    logits = S.f32_to_bf16_bits((rng.standard_normal((6, 128)) * 3).astype(np.float32))
+    p32 = O.softmax_rows(logits)
+
+    def rb(v):
+        return float(S.bf16_bits_to_f32(S.f32_to_bf16_bits(np.array([v], np.float32)))[0])
+
+    with O.softmax_precision("bf16"):
+        p16 = O.softmax_rows(logits)
+    assert np.array_equal(O.softmax_rows(logits), p32), "the switch must restore the default"
+    lf = S.bf16_bits_to_f32(logits)
+    for r in range(logits.shape[0]):
+        m = float(lf[r].max())
+        e = [rb(O.exp(rb(float(v) - m))) for v in lf[r]]
+        s = 0.0
+        for v in e:
+            s = rb(np.float32(s) + np.float32(v))
+        inv = rb(np.float32(1.0) / np.float32(s))
+        want = S.f32_to_bf16_bits(np.array([np.float32(v) * np.float32(inv) for v in e], np.float32))
+        assert np.array_equal(p16[r], want), f"row {r}"
+    assert not np.array_equal(p16, p32), "the two precisions should differ on these rows"
+    # the block route runs under the switch too (weights move by at most a few bf16 ulps)
+    bw = S.host_block(S.QWEN3_30B_A3B, 1)
+    x = S.host_x(7, 4, S.QWEN3_30B_A3B.hidden)
+    i32, w32, _, _ = O.route(bw, x)
+    with O.softmax_precision("bf16"):
+        i16, w16, _, _ = O.route(bw, x)
+    d = np.abs(S.bf16_bits_to_f32(w16) - S.bf16_bits_to_f32(w32))
+    assert d.max() < 0.05, d.max()
