@@ -303,7 +303,10 @@ __global__ void __launch_bounds__(128) route_fused_kernel(RouterArgs ra, TopkArg
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t0 = blockIdx.y * NT;
   pdl_wait();
-  pdl_trigger();
+  // no early launch_dependents: the next kernel's CTAs (the GEMV: 512 threads, ~200 KB of
+  // shared memory) would wait resident on the SMs this kernel's later CTAs need (measured:
+  // a Qwen3 T=64 block 167.9 us with the early trigger, 157.7 us without); every CTA's
+  // exit counts as its trigger
   router_tile<NE, NT>(ra, (blockIdx.x * 4 + warp) * NE, t0, lane);
   __threadfence();
   __syncthreads();
