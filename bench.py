@@ -11,7 +11,8 @@ timed step.
          resident in HBM (max over ranks)
   e2e    tokens/s through the public API (SparseMoeBlock.forward, or
          ExpertParallelBlock.forward under torchrun) from pinned host memory: H2D copy
-         of x, block, D2H copy of the output, per step
+         of x, block, D2H copy of the output, per step; the timed steps are issued back
+         to back and the host waits once
   roofline  the dominant kernel (largest per-stage device time) against the measured
          HBM copy bandwidth (decode) or bf16 tensor peak (prefill)
   cpu_baseline  the CPU oracle (C restatement of the reference block) on the host cores
@@ -353,28 +354,102 @@ def events():
 
 
 def e2e_run(args, fwd, xs_host_bits, out_shape, dev, timer, graphed=None):
-    """Mean ms of H2D (pinned) + forward + D2H per step, max over ranks. With `graphed`
-    (a graph.GraphedForward), each step copies the host tokens straight into its input
+    """ms per step of H2D (pinned) + forward + D2H, max over ranks: the K steps are issued
+    back to back on the stream, each with its own host-to-device copy of that step's
+    tokens and device-to-host copy of its output, and the host waits once at the end (a
+    serving loop that does not stall the GPU between steps; per-step synchronisation
+    would add the host's submission latency to every step). With `graphed` (a
+    graph.GraphedForward), each step copies the host tokens straight into its input
     buffer and replays it: the public decode-step API."""
     import numpy as np
     import torch
     stream = torch.cuda.current_stream(dev)
     xs_pin = [torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).pin_memory() for x in xs_host_bits]
-    out_pin = torch.empty(*out_shape, dtype=torch.bfloat16).pin_memory()
+    outs_pin = [torch.empty(*out_shape, dtype=torch.bfloat16).pin_memory() for _ in range(args.steps)]
     xdev = graphed.static_x if graphed is not None else torch.empty(xs_pin[0].shape, dtype=torch.bfloat16,
                                                                      device=dev)
-    times = []
-    for i in range(args.warmup + args.steps):
-        a, b = events()
-        a.record(stream)
+
+    if graphed is not None:
+        return e2e_pipelined(args, graphed, xs_pin, outs_pin, dev, timer)
+
+    def step(i, out_pin):
         xdev.copy_(xs_pin[i % len(xs_pin)], non_blocking=True)
-        y = graphed.replay() if graphed is not None else fwd(xdev)
+        y = fwd(xdev)
         out_pin.copy_(y, non_blocking=True)
-        b.record(stream)
-        b.synchronize()
-        if i >= args.warmup:
-            times.append(a.elapsed_time(b))
-    return timer.max_over_ranks(statistics.mean(times))
+
+    for i in range(args.warmup):
+        step(i, outs_pin[0])
+    torch.cuda.synchronize(dev)
+    a, b = events()
+    a.record(stream)
+    for i in range(args.steps):
+        step(args.warmup + i, outs_pin[i])
+    b.record(stream)
+    b.synchronize()
+    return timer.max_over_ranks(a.elapsed_time(b) / args.steps)
+
+
+def e2e_pipelined(args, graphed, xs_pin, outs_pin, dev, timer):
+    """e2e through a graph.GraphedForward with the copies overlapped with compute: step
+    i's tokens go host -> device on an upload stream into one of two staging buffers while
+    step i-1 computes; the compute stream copies them into the graph's input, replays, and
+    copies the output into one of two output stages, which a download stream copies to the
+    step's pinned host buffer. Every step still moves its tokens up and its output down."""
+    import torch
+    comp = torch.cuda.current_stream(dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    xdev, ydev = graphed.static_x, graphed.static_y
+    stage = [torch.empty_like(xdev) for _ in range(2)]
+    ostage = [torch.empty_like(ydev) for _ in range(2)]
+
+    def run(n, first, outs):
+        ev = lambda: torch.cuda.Event()  # noqa: E731
+        h_ev, c_ev, d_ev = [ev() for _ in range(n)], [ev() for _ in range(n)], [ev() for _ in range(n)]
+
+        def upload(i):
+            with torch.cuda.stream(up):
+                if i >= 2:
+                    up.wait_event(c_ev[i - 2])  # step i-2 has read stage[i % 2]
+                stage[i % 2].copy_(xs_pin[(first + i) % len(xs_pin)], non_blocking=True)
+                h_ev[i].record(up)
+
+        upload(0)
+        if n > 1:
+            upload(1)
+        for i in range(n):
+            comp.wait_event(h_ev[i])
+            xdev.copy_(stage[i % 2], non_blocking=True)
+            y = graphed.replay()
+            if i >= 2:
+                comp.wait_event(d_ev[i - 2])  # the output stage is free again
+            ostage[i % 2].copy_(y, non_blocking=True)
+            c_ev[i].record(comp)
+            with torch.cuda.stream(down):
+                down.wait_event(c_ev[i])
+                outs[i].copy_(ostage[i % 2], non_blocking=True)
+                d_ev[i].record(down)
+            if i + 2 < n:
+                upload(i + 2)
+        return d_ev[n - 1]
+
+    run(max(1, args.warmup), 0, [outs_pin[0]] * max(1, args.warmup))
+    torch.cuda.synchronize(dev)
+    a, _ = events()
+    a.record(comp)
+    up.wait_stream(comp)
+    last = run(args.steps, args.warmup, outs_pin)
+    b = torch.cuda.Event(enable_timing=True)
+    down.wait_event(last)
+    b.record(down)
+    b.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    # the pipelined outputs are the steps' own: first and last timed step against a
+    # synchronous replay of the same tokens, bit for bit
+    for i in (0, args.steps - 1):
+        want = graphed(xs_pin[(args.warmup + i) % len(xs_pin)].to(dev)).cpu()
+        if not torch.equal(want.view(torch.int16), outs_pin[i].view(torch.int16)):
+            raise RuntimeError(f"pipelined e2e: step {i} output differs from a synchronous replay")
+    return timer.max_over_ranks(ms)
 
 
 def hbm_roofline(name, alg_bytes, launch_ms, extra=None):
@@ -685,7 +760,8 @@ def run_block(args, dev):
 
     # end to end through the public API: the block captured once (graph.GraphedForward)
     # and replayed per step, host tokens in and the step's output back every step
-    e2e_api = "graph.GraphedForward(SparseMoeBlock.forward), pinned H2D + replay + D2H per step"
+    e2e_api = ("graph.GraphedForward(SparseMoeBlock.forward), pinned H2D + replay + D2H per step, "
+               "the copies of neighbouring steps overlapped with compute on upload / download streams")
     graphed = None
     if not args.no_graph:
         try:
@@ -696,7 +772,7 @@ def run_block(args, dev):
             graphed = None
             e2e_api = f"SparseMoeBlock.forward eager (graph capture failed: {type(ex).__name__})"
     if graphed is None and args.no_graph:
-        e2e_api = "SparseMoeBlock.forward eager, pinned H2D + forward + D2H per step"
+        e2e_api = "SparseMoeBlock.forward eager, pinned H2D + forward + D2H per step, steps issued back to back"
     e2e = e2e_run(args, lambda xd: blk.forward(xd, out), xs_host, (T, H), dev, timer, graphed)
 
     sweep = {}
