@@ -1006,9 +1006,13 @@ cudaError_t launch_qgemv(const QgemvArgs& a, bool gated, int slots, int rows_per
   // fill the GPU; narrow units in 4-warp CTAs otherwise, for parallelism.
   const int rows2 = gated ? 16 : 32;
   const bool wide = (long long)slots * ((a.N + rows2 - 1) / rows2) >= 148 * 16;
-  // Tokens per pass over an expert's weights: 8, 16 or 32 by the expected rows per
-  // expert (an expert with more rows takes more passes), while the staged rows fit.
-  int nc = rows_per_expert > 16 ? 4 : rows_per_expert > 8 ? 2 : 1;
+  // Tokens per pass over an expert's weights: 8 up to 16 expected rows per expert, 32
+  // above (an expert with more rows takes more passes), while the staged rows fit; 16 only
+  // when 32 do not fit. Measured on the B200 (Qwen3-30B-A3B shapes, graph-replayed blocks):
+  // up to 16 expected rows, 8-token passes of the whole-K-scale kernel beat 16-token passes
+  // (T=96: 172 against 211 us; T=192: 248 against 262 us), and above 16 rows 32-token
+  // passes beat 16-token ones (T=320: 341 against 365 us).
+  int nc = rows_per_expert > 16 ? 4 : 1;
   while (nc > 1 && (size_t)kTok * nc * (2 * a.K + 16) > 140 * 1024) nc >>= 1;
   if (gated) {
     if (nc == 4) return launch_qgemv_nc<true, 4>(a, slots, wide, st);
