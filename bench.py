@@ -353,6 +353,22 @@ def events():
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
 
+class GraphAdapter:
+    """A captured torch.cuda.CUDAGraph with its static input and output, used like a
+    graph.GraphedForward by e2e_run."""
+
+    def __init__(self, graph, static_x, static_y):
+        self.graph, self.static_x, self.static_y = graph, static_x, static_y
+
+    def replay(self):
+        self.graph.replay()
+        return self.static_y
+
+    def __call__(self, x):
+        self.static_x.copy_(x)
+        return self.replay()
+
+
 def e2e_run(args, fwd, xs_host_bits, out_shape, dev, timer, graphed=None):
     """ms per step of H2D (pinned) + forward + D2H, max over ranks: the K steps are issued
     back to back on the stream, each with its own host-to-device copy of that step's
@@ -920,7 +936,9 @@ def run_ep_block(args, world, rank, local, dev):
         roof = hbm_roofline("ep experts (gate/up + down)", n_act * wb["per_expert"], stage_ms["experts"],
                             {"stage_ms": stage_ms, "local_experts_touched": n_act})
     roof["rank"] = 0  # rank 0's own experts and their device time
-    e2e = e2e_run(args, lambda xd: blk.forward(xd, out), xs_host, (T, H), dev, timer)
+    # e2e through the captured block (its NCCL calls inside) when there is one
+    e2e = e2e_run(args, lambda xd: blk.forward(xd, out), xs_host, (T, H), dev, timer,
+                  GraphAdapter(graph, static_x, out) if graph is not None else None)
     del graph  # holds NCCL work: released before the process group is destroyed
     launches = 4 + 2 + group_launches(P_all, n)
     return {
