@@ -553,23 +553,24 @@ __global__ void __launch_bounds__(FK ? 512 : 256) qgemv_kernel(QgemvArgs a, int 
   }
 }
 
-// Integer path (decode, whole-K scales, MT = 2, 4 tokens per pass): weights enter the MMA
+// Integer path (decode, whole-K scales, MT = 2, 8 tokens per pass): weights enter the MMA
 // as u8 nibbles (w & 0x0f0f0f0f even nibbles, (w >> 4) & 0x0f0f0f0f odd nibbles), tokens as
 // two s8 limbs of a per-token fixed-point mantissa m = rint(x * 2^-E), |m| < 2^14,
-// m = 128 * hi + lo, lo in [0, 127]. MMA columns n = 2t + limb (t = token 0..3), so a
-// lane's C fragment holds one token's (hi, lo) sums for rows gq and gq+8:
+// m = 128 * hi + lo, lo in [0, 127]. Two column chunks of 8 MMA columns; in chunk n,
+// column 2t + limb holds token 4n + t (t = 0..3), so a lane's C fragment of chunk n holds
+// token 4n + cq's (hi, lo) sums for rows gq and gq+8 (the weight fragments serve both):
 //   sum_k x*(s*q + b) = 2^E * (s * (128*D_hi + D_lo) + b * X'),  X' = sum_k m.
 // k-permutation per 32-k MMA (word 2cq for MMA 0, 2cq+1 for MMA 1 of a group): k-slots
 // 4cq+i hold element 16cq + 2i (+8 for MMA 1), k-slots 16+4cq+i element 16cq + 2i + 1.
-// Shared memory: xq [8 columns][K + 64 B] s8 limbs in fragment order, xs [G][4] float X',
-// emax [4] int, scale regions (as FK), rings (weights only).
+// Shared memory: xq [16 columns][K + 64 B] s8 limbs in fragment order, xs [G][8] float X',
+// emax [8] int, scale regions (as FK), rings (weights only).
 template <bool GATED>
 __global__ void __launch_bounds__(512) qgemv_i8_kernel(QgemvArgs a, int units_per_expert, int ctas_per_expert,
                                                        int max_slots) {
   constexpr int MT = 2, NS = 2;
   constexpr int ROWS = GATED ? 8 * MT : 16 * MT;
-  constexpr int TOK = 4;
-  constexpr int kCols = 8;
+  constexpr int TOK = 8;
+  constexpr int kCols = 16;
   constexpr int kRingRows = MT * 16;
   constexpr int kStageBytes = kRingRows * kKC * 32;
   constexpr int kPieces = kRingRows * kKC * 2 / 32;
@@ -597,7 +598,7 @@ __global__ void __launch_bounds__(512) qgemv_i8_kernel(QgemvArgs a, int units_pe
   const uint32_t xs_s = xq_s + kCols * col_bytes;
   float* xs = reinterpret_cast<float*>(smem + kCols * col_bytes);           // [G][TOK]
   int* emax = reinterpret_cast<int*>(smem + kCols * col_bytes + G * TOK * 4);  // [TOK]
-  const uint32_t sreg_all = xs_s + G * TOK * 4 + 16;
+  const uint32_t sreg_all = xs_s + G * TOK * 4 + TOK * 4;  // after emax [TOK] (16-byte multiple)
   const uint32_t sreg_s = sreg_all + (uint32_t)(warp * kRingRows * G * 4);
   const uint32_t ring_s = sreg_all + (uint32_t)(nwarps * kRingRows * G * 4) + (uint32_t)(warp * NS * kStageBytes);
 
@@ -730,7 +731,8 @@ __global__ void __launch_bounds__(512) qgemv_i8_kernel(QgemvArgs a, int units_pe
 #pragma unroll
         for (int limb = 0; limb < 2; ++limb) {
           const uint4 o = make_uint4(pack(0, limb), pack(1, limb), pack(8, limb), pack(9, limb));
-          *reinterpret_cast<uint4*>(smem + (size_t)(2 * t + limb) * col_bytes + g * 64 + c * 16) = o;
+          // token t: chunk t / 4, column 2 (t % 4) + limb of the chunk
+          *reinterpret_cast<uint4*>(smem + (size_t)(8 * (t >> 2) + 2 * (t & 3) + limb) * col_bytes + g * 64 + c * 16) = o;
         }
         if (c == 0) xs[g * TOK + t] = (float)xsum;
       }
@@ -741,9 +743,11 @@ __global__ void __launch_bounds__(512) qgemv_i8_kernel(QgemvArgs a, int units_pe
     if (!unit_live) continue;
 
     const uint32_t xb = xq_s + gq * col_bytes + cq * 16;  // column gq's fragment base
-    float acc[MT][2];  // [tile][row gq / gq+8], token cq
+    float acc[MT][2][2];  // [tile][chunk n: token 4n + cq][row gq / gq+8]
 #pragma unroll
-    for (int t = 0; t < MT; ++t) acc[t][0] = acc[t][1] = 0.0f;
+    for (int t = 0; t < MT; ++t)
+#pragma unroll
+      for (int n = 0; n < 2; ++n) acc[t][n][0] = acc[t][n][1] = 0.0f;
     for (int c = 0; c < nchunks; ++c) {
       if (c + 1 < nchunks) issue_chunk(c + 1);
       else cp_commit();
@@ -765,19 +769,23 @@ __global__ void __launch_bounds__(512) qgemv_i8_kernel(QgemvArgs a, int units_pe
 #pragma unroll
       for (int gl = 0; gl < kKC; ++gl) {
         const int g = g0 + gl;
-        const uint4 bf = lds_u4(xb + g * 64);           // (b0, b1) of MMA 0, (b0, b1) of MMA 1
-        const float X = xs[g * TOK + cq];
+        uint4 bf[2];  // per column chunk: (b0, b1) of MMA 0, (b0, b1) of MMA 1
+        float X[2];
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+          bf[n] = lds_u4(xb + n * 8 * col_bytes + g * 64);
+          X[n] = xs[g * TOK + 4 * n + cq];
+        }
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
           const int rr = t * 16 + gq;
           const uint32_t off = ((gl ^ (rr & 3)) * 32) + cq * 8;
           const uint2 wlo = lds_u2(st + rr * (kKC * 32) + off);
           const uint2 whi = lds_u2(st + (rr + 8) * (kKC * 32) + off);
-          int d[4];
-          imma(d, wlo.x & 0x0f0f0f0fu, whi.x & 0x0f0f0f0fu, (wlo.x >> 4) & 0x0f0f0f0fu, (whi.x >> 4) & 0x0f0f0f0fu,
-               bf.x, bf.y, true);
-          imma(d, wlo.y & 0x0f0f0f0fu, whi.y & 0x0f0f0f0fu, (wlo.y >> 4) & 0x0f0f0f0fu, (whi.y >> 4) & 0x0f0f0f0fu,
-               bf.z, bf.w, false);
+          const uint32_t a0 = wlo.x & 0x0f0f0f0fu, a1 = whi.x & 0x0f0f0f0fu;
+          const uint32_t a2 = (wlo.x >> 4) & 0x0f0f0f0fu, a3 = (whi.x >> 4) & 0x0f0f0f0fu;
+          const uint32_t a4 = wlo.y & 0x0f0f0f0fu, a5 = whi.y & 0x0f0f0f0fu;
+          const uint32_t a6 = (wlo.y >> 4) & 0x0f0f0f0fu, a7 = (whi.y >> 4) & 0x0f0f0f0fu;
           const uint32_t s_lo2 = (gl >> 1) ? sw[t][0].y : sw[t][0].x;
           const uint32_t s_hi2 = (gl >> 1) ? sw[t][1].y : sw[t][1].x;
           const uint32_t b_lo2 = (gl >> 1) ? bw[t][0].y : bw[t][0].x;
@@ -786,19 +794,27 @@ __global__ void __launch_bounds__(512) qgemv_i8_kernel(QgemvArgs a, int units_pe
           const float s_h = (gl & 1) ? bf_hi(s_hi2) : bf_lo(s_hi2);
           const float b_l = (gl & 1) ? bf_hi(b_lo2) : bf_lo(b_lo2);
           const float b_h = (gl & 1) ? bf_hi(b_hi2) : bf_lo(b_hi2);
-          // (hi, lo) sums of token cq: c0/c1 row gq, c2/c3 row gq+8 (exact below 2^24)
-          const float v_l = __fmaf_rn(128.0f, i2f(d[0]), i2f(d[1]));
-          const float v_h = __fmaf_rn(128.0f, i2f(d[2]), i2f(d[3]));
-          acc[t][0] = __fmaf_rn(b_l, X, __fmaf_rn(s_l, v_l, acc[t][0]));
-          acc[t][1] = __fmaf_rn(b_h, X, __fmaf_rn(s_h, v_h, acc[t][1]));
+#pragma unroll
+          for (int n = 0; n < 2; ++n) {
+            int d[4];
+            imma(d, a0, a1, a2, a3, bf[n].x, bf[n].y, true);
+            imma(d, a4, a5, a6, a7, bf[n].z, bf[n].w, false);
+            // (hi, lo) sums of token 4n + cq: c0/c1 row gq, c2/c3 row gq+8 (exact below 2^24)
+            const float v_l = __fmaf_rn(128.0f, i2f(d[0]), i2f(d[1]));
+            const float v_h = __fmaf_rn(128.0f, i2f(d[2]), i2f(d[3]));
+            acc[t][n][0] = __fmaf_rn(b_l, X[n], __fmaf_rn(s_l, v_l, acc[t][n][0]));
+            acc[t][n][1] = __fmaf_rn(b_h, X[n], __fmaf_rn(s_h, v_h, acc[t][n][1]));
+          }
         }
       }
       __syncwarp();
     }
     cp_wait<0>();
     pdl_trigger();
-    // ---- epilogue: token cq, rows gq / gq+8 of each tile; undo 2^-E
-    const int tok = cq;
+    // ---- epilogue: tokens cq and 4 + cq, rows gq / gq+8 of each tile; undo 2^-E
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+    const int tok = 4 * n + cq;
     if (tok < ntok) {
       const int mb = emax[tok];
       int sh = 0;
@@ -818,14 +834,15 @@ __global__ void __launch_bounds__(512) qgemv_i8_kernel(QgemvArgs a, int units_pe
         if (GATED) {
           const int row = r0 + 8 * t + gq;
           if (row < N)
-            o[row] = a.act ? gelu_mul_bf16(rbf(acc[t][0] * us), rbf(acc[t][1] * us))
-                           : swiglu_bf16(rbf(acc[t][0] * us), rbf(acc[t][1] * us));
+            o[row] = a.act ? gelu_mul_bf16(rbf(acc[t][n][0] * us), rbf(acc[t][n][1] * us))
+                           : swiglu_bf16(rbf(acc[t][n][0] * us), rbf(acc[t][n][1] * us));
         } else {
           const int row = r0 + 16 * t + gq;
-          if (row < N) o[row] = f2bf(acc[t][0] * us);
-          if (row + 8 < N) o[row + 8] = f2bf(acc[t][1] * us);
+          if (row < N) o[row] = f2bf(acc[t][n][0] * us);
+          if (row + 8 < N) o[row + 8] = f2bf(acc[t][n][1] * us);
         }
       }
+    }
     }
   }
 }
@@ -968,7 +985,7 @@ static cudaError_t launch_i8(const QgemvArgs& a, int slots, int wpc, cudaStream_
   const int cpe = (upe + wpc - 1) / wpc;
   const long long blocks = (long long)cpe * slots;
   const int G = a.K / 64;
-  const size_t smem = (size_t)8 * (a.K + 64) + (size_t)G * 4 * 4 + 16 + (size_t)wpc * 32 * G * 4 +
+  const size_t smem = (size_t)16 * (a.K + 64) + (size_t)G * 8 * 4 + 32 + (size_t)wpc * 32 * G * 4 +
                       (size_t)wpc * 2 * 32 * kKC * 32;
   if (smem > 227 * 1024 || blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   static thread_local int set_dev = -1;
