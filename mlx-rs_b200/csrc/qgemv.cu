@@ -29,6 +29,7 @@
 // 16c+8+j, 16c+12+j. The staged token rows are stored in exactly that order, so a
 // lane's B fragments for a group are two 16-byte shared loads.
 #include <algorithm>
+#include <cmath>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -1001,7 +1002,7 @@ static cudaError_t launch_i8(const QgemvArgs& a, int slots, int wpc, cudaStream_
 }
 
 template <bool GATED, int NC>
-static cudaError_t launch_qgemv_nc(const QgemvArgs& a, int slots, bool wide, cudaStream_t st) {
+static cudaError_t launch_qgemv_nc(const QgemvArgs& a, int slots, bool wide, double active, cudaStream_t st) {
   {
     const char* env = std::getenv("MOE_B200_GEMV_I8");  // prototype: integer MMA path
     if (env && env[0] == '1' && NC == 1 && wide && (a.K / 64) % 4 == 0) {
@@ -1011,6 +1012,24 @@ static cudaError_t launch_qgemv_nc(const QgemvArgs& a, int slots, bool wide, cud
   }
   if (NC == 1 && wide) {
     const int fw = fk_warps(a, GATED);
+    // Long-K gated launches (16-warp CTAs of two-tile units by default): unit size and CTA
+    // shape by the expected grid (all three forms give identical bits). Measured on the
+    // B200, gate/up launch of graph-replayed blocks:
+    //  - the two-tile grid fills at most ~1.25 waves: one-tile units in 8-warp CTAs, two per
+    //    SM (Qwen3-30B-A3B T=8 48.0 -> 42.5 us; LFM2-8B-A1B T=8 28.7 -> 22.6 us);
+    //  - an expert spans 5 or more 16-warp CTAs (N >= 1280): one-tile units in 16-warp CTAs
+    //    with 4-chunk rings (LFM2 T=32 / 64 / 128: 66.5 / 111.5 / 88.0 -> 56.3 / 85.0 /
+    //    70.7 us);
+    //  - otherwise two-tile units (Qwen3 T=32 / 64: 73.7 / 91.1 us; one-tile units took
+    //    74.8-78.9 / 91.2-95.2).
+    if (GATED && fw == 16) {
+      const int upe2 = (a.N + 15) / 16;
+      const double ctas2 = active * ((upe2 + 15) / 16);
+      if (ctas2 <= 1.25 * 148 && 2 * (qgemv_smem<1, 1, 2, true>(a.K, 8) + 1024) <= 228 * 1024)
+        return launch_qgemv_t<GATED, 1, 1, 2, true>(a, slots, 8, st);
+      if (upe2 >= 80 && qgemv_smem<1, 1, 4, true>(a.K, 16) <= 227 * 1024)
+        return launch_qgemv_t<GATED, 1, 1, 4, true>(a, slots, 16, st);
+    }
     if (fw) return launch_qgemv_t<GATED, 2, 1, 2, true>(a, slots, fw, st);
   }
   return wide ? launch_qgemv_t<GATED, 2, NC, 2>(a, slots, 8, st) : launch_qgemv_t<GATED, 1, NC, 4>(a, slots, 4, st);
@@ -1031,14 +1050,18 @@ cudaError_t launch_qgemv(const QgemvArgs& a, bool gated, int slots, int rows_per
   // passes beat 16-token ones (T=320: 341 against 365 us).
   int nc = rows_per_expert > 16 ? 4 : 1;
   while (nc > 1 && (size_t)kTok * nc * (2 * a.K + 16) > 140 * 1024) nc >>= 1;
+  // expected experts with rows: slots * rows_per_expert rows spread over the experts
+  const int E = a.num_experts_total > 0 ? a.num_experts_total : slots;
+  const double active =
+      std::min<double>(slots, E * (1.0 - std::exp(-(double)slots * rows_per_expert / E)));
   if (gated) {
-    if (nc == 4) return launch_qgemv_nc<true, 4>(a, slots, wide, st);
-    if (nc == 2) return launch_qgemv_nc<true, 2>(a, slots, wide, st);
-    return launch_qgemv_nc<true, 1>(a, slots, wide, st);
+    if (nc == 4) return launch_qgemv_nc<true, 4>(a, slots, wide, active, st);
+    if (nc == 2) return launch_qgemv_nc<true, 2>(a, slots, wide, active, st);
+    return launch_qgemv_nc<true, 1>(a, slots, wide, active, st);
   }
-  if (nc == 4) return launch_qgemv_nc<false, 4>(a, slots, wide, st);
-  if (nc == 2) return launch_qgemv_nc<false, 2>(a, slots, wide, st);
-  return launch_qgemv_nc<false, 1>(a, slots, wide, st);
+  if (nc == 4) return launch_qgemv_nc<false, 4>(a, slots, wide, active, st);
+  if (nc == 2) return launch_qgemv_nc<false, 2>(a, slots, wide, active, st);
+  return launch_qgemv_nc<false, 1>(a, slots, wide, active, st);
 }
 
 }  // namespace moe
