@@ -667,6 +667,14 @@ bool ensure_side(moe_ctx* ctx) {
   return true;
 }
 
+// The GEMV chain and the tcgen05 chain own disjoint experts from gate/up through down
+// (both kernels on both projections, with one row threshold): only then may they run on
+// two streams. With one projection on a single kernel for all experts, that projection
+// reads rows the other chain's first projection writes, so the steps run in order.
+bool split_chains(const ExpertPlan& p) {
+  return p.tc_gu && p.tc_dn && p.gemv_gu && p.gemv_dn && p.gemv_skip_gu == p.gemv_skip_dn;
+}
+
 int run_routed_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weights* wts, const void* x,
                        int64_t T, const BlockWs& ws, const ExpertPlan& plan, cudaEvent_t* ev, int act) {
   const int E = cfg->num_experts, H = cfg->hidden, I = cfg->moe_inter, k = cfg->top_k;
@@ -697,8 +705,7 @@ int run_routed_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_bloc
   // sizes) stay off the GEMV's dependency chain: measured 4-6 us per Qwen3 block at
   // T = 16..96. Sequential under moe_block_profile (stage events) and until the side
   // stream exists.
-  const bool fork = ev == nullptr && (plan.tc_gu || plan.tc_dn) && (plan.gemv_gu || plan.gemv_dn) &&
-                    ensure_side(ctx);
+  const bool fork = ev == nullptr && split_chains(plan) && ensure_side(ctx);
   cudaStream_t tcs = fork ? ctx->side : ctx->stream;
   if (fork) {
     MOE_CUDA(ctx, cudaEventRecord(ctx->fork_ev, ctx->stream));
@@ -1353,7 +1360,7 @@ int ep_experts(moe_ctx* ctx, const moe_block_config* cfg, const moe_block_weight
   gu.part_rows = P;
   gu.num_experts_total = El;
   // hybrid step: the tcgen05 chain on the side stream, as in run_routed_experts
-  const bool fork = (plan.tc_gu || plan.tc_dn) && (plan.gemv_gu || plan.gemv_dn) && ensure_side(ctx);
+  const bool fork = split_chains(plan) && ensure_side(ctx);
   cudaStream_t tcs = fork ? ctx->side : ctx->stream;
   if (fork) {
     MOE_CUDA(ctx, cudaEventRecord(ctx->fork_ev, ctx->stream));

@@ -460,6 +460,26 @@ def test_extreme_shapes_match_oracle(cfg, T):
     _live(cfg, 31, T)
 
 
+@pytest.mark.parametrize("cfg,T", [
+    # I % 128 != 0: gate/up on the GEMV for every expert, down hybrid (tcgen05 from 32 rows)
+    (S.MoeConfig(256, 8, 2, 192, 0, S.SCORING_SOFTMAX_BIAS, True, False, name="gemv-gate-up-hybrid-down"), 80),
+    # H % 128 != 0: gate/up hybrid, down on the GEMV for every expert
+    (S.MoeConfig(192, 8, 2, 128, 0, S.SCORING_SOFTMAX_BIAS, True, False, name="hybrid-gate-up-gemv-down"), 80),
+])
+def test_hybrid_with_one_projection_on_one_kernel(cfg, T):
+    """Hybrid steps where only one projection's shape suits the tensor-core kernel: the
+    other projection reads rows of every expert, so the two kernels' chains must not run
+    on separate streams; outputs against the oracle, routing bit-exact. Skewed routing
+    (per-expert selection bias) gives some experts 32 rows or more while the rows stay
+    under 24 per expert on average, so both kernels run (the tensor-core tolerance)."""
+    import oracle as O
+    bw, _ = _block(cfg, 41, 1.0)
+    idx = O.block_forward(bw, S.host_x(41, T, cfg.hidden))[1]
+    cnt = np.bincount(idx.ravel(), minlength=cfg.num_experts)
+    assert cnt.max() >= 32 and cnt.min() < 32 and idx.size < 24 * cfg.num_experts
+    _live(cfg, 41, T, bias_std=1.0, ulp_tol=ULP_TOL_TC)
+
+
 @pytest.mark.parametrize("cfg_name,seed,T", [("QWEN3_30B_A3B", 1, 64), ("LFM2_8B_A1B", 3, 32)])
 def test_int8_gemv_path_matches_oracle(cfg_name, seed, T, monkeypatch):
     """The opt-in integer decode GEMV (u8 weights, two s8 limbs of each token row, int32
