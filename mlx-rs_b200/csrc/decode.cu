@@ -34,6 +34,7 @@
 // (the outputs are then invalid and moe_ctx_status reports it). The launch is cooperative,
 // which guarantees that every CTA of the grid is resident, so the barrier cannot wait on a
 // CTA that has not started.
+#include <algorithm>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -44,14 +45,16 @@ namespace moe {
 
 namespace {
 
-constexpr int kThreads = kDecodeWarps * 32;
 constexpr int kKC = 4;                        // groups of 64 per ring chunk
 constexpr int kRowBytes = kKC * 32;           // one weight row's bytes per chunk
 constexpr int kSOff = 16 * kRowBytes;         // scales of a stage: [16 rows][4] bf16
 constexpr int kBOff = kSOff + 16 * kKC * 2;   // biases of a stage
 constexpr int kStage = kBOff + 16 * kKC * 2;  // 2304 bytes
-constexpr int kNS2 = 8;                       // gate/up ring stages per warp (HBM stream)
-constexpr int kNS3 = 4;                       // down ring stages per warp (from L2)
+// Ring stages per warp: gate/up (HBM stream) and down (from L2). 8-warp CTAs hold the
+// whole K of a unit in flight; 16-warp CTAs (for more units than 8 warps per SM cover)
+// half of it.
+__host__ __device__ constexpr int ns2_of(int warps) { return warps == 16 ? 4 : 8; }
+__host__ __device__ constexpr int ns3_of(int warps) { return warps == 16 ? 2 : 4; }
 constexpr uint64_t kWaitNs = 200ull * 1000 * 1000;
 constexpr size_t kMaxSmem = 224 * 1024;  // dynamic; the static arrays below take ~1.2 KB
 
@@ -61,13 +64,13 @@ struct DSmem {
 __host__ __device__ inline uint32_t al16(uint32_t v) { return (v + 15u) & ~15u; }
 // Phases 1-2 and phase 3 reuse the same dynamic shared memory; the top-k scratch (tk)
 // lives in the phase-2 rings, which are idle until the top-k is done.
-__host__ __device__ inline DSmem dsmem(int T, int P, int E, int H, int I, int Is) {
+__host__ __device__ inline DSmem dsmem(int T, int P, int E, int H, int I, int Is, int warps) {
   DSmem m{};
   uint32_t o = 0;
   m.xr = o;    o = al16(o + (uint32_t)T * H * 2);              // raw token rows (swizzled pieces)
   m.x = o;     o = al16(o + (uint32_t)T * (2 * H + 16));       // token rows, fragment order
   m.xsum = o;  o = al16(o + (uint32_t)(H / 64) * 8 * 4);       // [G_H][8] group sums
-  m.ring2 = o; o = al16(o + (uint32_t)kDecodeWarps * kNS2 * kStage);
+  m.ring2 = o; o = al16(o + (uint32_t)warps * ns2_of(warps) * kStage);
   m.end2 = o;
   m.tk = m.ring2;                                              // [2][T][E] f32 + [16] + [2][P]
   o = 0;
@@ -76,8 +79,8 @@ __host__ __device__ inline DSmem dsmem(int T, int P, int E, int H, int I, int Is
   m.hs = o;    o = al16(o + (Is ? (uint32_t)T * (2 * Is + 16) : 0u));
   m.hssum = o; o = al16(o + (Is ? (uint32_t)(Is / 64) * 8 * 4 : 0u));
   m.prod = o;  o = al16(o + (uint32_t)P * 16 * 4);             // bf16(y * w) per pair, 16 rows
-  m.spart = o; o = al16(o + (Is ? (uint32_t)kDecodeWarps * 8 * 16 * 4 : 0u));
-  m.ring3 = o; o = al16(o + (uint32_t)kDecodeWarps * kNS3 * kStage);
+  m.spart = o; o = al16(o + (Is ? (uint32_t)warps * 8 * 16 * 4 : 0u));
+  m.ring3 = o; o = al16(o + (uint32_t)warps * ns3_of(warps) * kStage);
   m.end3 = o;
   (void)E;
   return m;
@@ -196,7 +199,7 @@ MOE_DEV void stage_rows(unsigned char* smem, uint32_t dst, float* sums, int sstr
   const int G = K >> 6;
   const int units = nrows * G * 4;
   const int rb = 2 * K + 16;
-  for (int u0 = 0; u0 < units; u0 += kThreads) {  // uniform trip count (shuffles below)
+  for (int u0 = 0; u0 < units; u0 += (int)blockDim.x) {  // uniform trip count (shuffles below)
     const int u = u0 + (int)threadIdx.x;
     const bool v = u < units;
     const int c = u & 3, g = (u >> 2) % G, t = (u >> 2) / G;
@@ -322,7 +325,7 @@ MOE_DEV void topk_cta(const TopkArgs& a, int T, float* vals, float* keys, float*
                       uint32_t* s_idx, uint16_t* s_w, uint16_t* s_gate, bool has_gate) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int E = a.E, n = T * E, k = a.k;
-  for (int i = tid; i < n; i += kThreads) {
+  for (int i = tid; i < n; i += (int)blockDim.x) {
     const int t = i / E, e = i - t * E;
     float v = bf2f(__ldcg(a.logits + (size_t)t * a.n_rows + e));
     if (a.scoring == 1) v = rbf(__fadd_rn(v, bf2f(a.expert_bias[e])));
@@ -345,7 +348,7 @@ MOE_DEV void topk_cta(const TopkArgs& a, int T, float* vals, float* keys, float*
       if (lane == 0) red[warp] = m;
     }
     __syncthreads();
-    for (int i = tid; i < n; i += kThreads) vals[i] = exp_canon(__fsub_rn(vals[i], red[i / E]));
+    for (int i = tid; i < n; i += (int)blockDim.x) vals[i] = exp_canon(__fsub_rn(vals[i], red[i / E]));
     __syncthreads();
     if (warp < T) {
       float sm = 0.0f;
@@ -355,7 +358,7 @@ MOE_DEV void topk_cta(const TopkArgs& a, int T, float* vals, float* keys, float*
       if (lane == 0) red[8 + warp] = sm;
     }
     __syncthreads();
-    for (int i = tid; i < n; i += kThreads) {
+    for (int i = tid; i < n; i += (int)blockDim.x) {
       const float v = rbf(__fdiv_rn(vals[i], red[8 + i / E]));
       vals[i] = v;
       keys[i] = v;
@@ -368,7 +371,7 @@ MOE_DEV void topk_cta(const TopkArgs& a, int T, float* vals, float* keys, float*
   // (index ascending among equal keys). The expert of rank r (the number of larger words
   // in its token's row) is the r-th winner of topk_token's arg-max rounds.
   uint32_t* ord = reinterpret_cast<uint32_t*>(keys);  // in place: [T][E]
-  for (int i = tid; i < n; i += kThreads) {
+  for (int i = tid; i < n; i += (int)blockDim.x) {
     const int e = i - (i / E) * E;
     const float kf = keys[i];
     uint32_t b = __float_as_uint(kf) >> 16;  // exact: keys are bf16 values
@@ -377,7 +380,7 @@ MOE_DEV void topk_cta(const TopkArgs& a, int T, float* vals, float* keys, float*
     ord[i] = (code << 16) | (0xffffu - (uint32_t)e);
   }
   __syncthreads();
-  for (int i = tid; i < n; i += kThreads) {
+  for (int i = tid; i < n; i += (int)blockDim.x) {
     const int t = i / E;
     const uint32_t* orow = ord + t * E;
     const uint32_t me = ord[i];
@@ -567,8 +570,9 @@ MOE_DEV void stream_units(const unsigned char* smem, uint32_t sbase, int first, 
   __syncwarp();
 }
 
-template <int NT>
-__global__ void __launch_bounds__(kThreads, 1) decode_block_kernel(DecodeArgs a) {
+template <int NT, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, 1) decode_block_kernel(DecodeArgs a) {
+  constexpr int kThreads = WARPS * 32, kNS2 = ns2_of(WARPS), kNS3 = ns3_of(WARPS);
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ uint32_t s_idx[kDecodeMaxP];
   __shared__ uint16_t s_w[kDecodeMaxP];
@@ -580,10 +584,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_block_kernel(DecodeArgs a)
   __shared__ int s_ok;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gq = lane >> 2, cq = lane & 3;
-  const int gw = blockIdx.x * kDecodeWarps + warp, W = gridDim.x * kDecodeWarps;
+  const int gw = blockIdx.x * WARPS + warp, W = gridDim.x * WARPS;
   const int T = a.T, k = a.k, P = T * k, H = a.H, I = a.I, Is = a.Is, E = a.ta.E;
   const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem);
-  const DSmem L = dsmem(T, P, E, H, I, Is);
+  const DSmem L = dsmem(T, P, E, H, I, Is, WARPS);
 
   // ---- phase 1: the token rows into shared memory, then router logits, one row per warp
   for (int i = tid; i < T * (H / 8); i += kThreads) {
@@ -800,8 +804,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_block_kernel(DecodeArgs a)
           }
         }
       };
-      const int count = warp < U ? (U - warp + kDecodeWarps - 1) / kDecodeWarps : 0;
-      stream_units<kNS3>(smem, sbase, warp, kDecodeWarps, count, 0, (GI + kKC - 1) / kKC, GI, I / 8, ring,
+      const int count = warp < U ? (U - warp + WARPS - 1) / WARPS : 0;
+      stream_units<kNS3>(smem, sbase, warp, WARPS, count, 0, (GI + kKC - 1) / kKC, GI, I / 8, ring,
                          a.scale8 != 0, rows_of, cols_of, epi);
     }
     if (Is) {
@@ -809,7 +813,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_block_kernel(DecodeArgs a)
       // added in warp order below)
       const int GS = Is / 64;
       const int nch = (GS + kKC - 1) / kKC;
-      const int cpw = (nch + kDecodeWarps - 1) / kDecodeWarps;
+      const int cpw = (nch + WARPS - 1) / WARPS;
       const int cb = warp * cpw, ce = cb + cpw < nch ? cb + cpw : nch;
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {  // zeros for a warp with no chunks
@@ -861,7 +865,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_block_kernel(DecodeArgs a)
       uint16_t o = f2bf(sacc);
       if (Is) {
         float ys = 0.0f;
-        for (int w = 0; w < kDecodeWarps; ++w) ys = __fadd_rn(ys, spart[(w * 8 + t) * 16 + r]);
+        for (int w = 0; w < WARPS; ++w) ys = __fadd_rn(ys, spart[(w * 8 + t) * 16 + r]);
         float sv = rbf(ys);
         if (a.has_gate) sv = rbf(__fmul_rn(sv, bf2f(s_gate[t])));
         o = f2bf(__fadd_rn(bf2f(o), sv));
@@ -873,28 +877,57 @@ __global__ void __launch_bounds__(kThreads, 1) decode_block_kernel(DecodeArgs a)
   }
 }
 
-template <int NT>
-cudaError_t launch_t(const DecodeArgs& a, size_t smem, cudaStream_t st) {
-  auto kern = decode_block_kernel<NT>;
+int sm_count() {
   static thread_local int set_dev = -1;
-  static thread_local int nsm = 0;
+  static thread_local int nsm = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nsm;
+  if (dev != set_dev) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0) nsm = n;
+    set_dev = dev;
+  }
+  return nsm;
+}
+
+// Warps per CTA: 16 when the gate/up units (the most distinct experts T tokens can select
+// times 16-row tiles, plus the shared expert's) outnumber 8 warps per SM, else 8, whose
+// rings hold a unit's whole K in flight. Measured on the B200 (graph-replayed blocks, L2
+// flushed): T=1 Qwen3-30B-A3B 768 units 32.8 us in 8-warp CTAs against 34.8-38.9 in
+// 16-warp ones, LFM2-8B-A1B 896 units 36.9 against 38.9-41.0; Qwen1.5-MoE 1408 units 51.2
+// against 47.1; T=2 Qwen3 / Qwen1.5 / LFM2 49.2 / 57.3 / 49.2 against 43.0 / 51.2 / 43.0.
+int decode_warps(int T, int k, int E, int I, int Is) {
+  const long long units = (long long)std::min(E, T * k) * (I / 8) + (Is ? Is / 8 : 0);
+  return units > 8LL * sm_count() ? 16 : 8;
+}
+
+size_t smem_for(int T, int k, int E, int H, int I, int Is, int warps) {
+  const int P = T * k;
+  const DSmem m = dsmem(T, P, E, H, I, Is, warps);
+  if (tk_bytes(T, P, E) > m.end2 - m.tk) return 0;
+  const size_t need = m.end2 > m.end3 ? m.end2 : m.end3;
+  return need <= kMaxSmem ? need : 0;
+}
+
+template <int NT, int WARPS>
+cudaError_t launch_t(const DecodeArgs& a, size_t smem, cudaStream_t st) {
+  auto kern = decode_block_kernel<NT, WARPS>;
+  static thread_local int set_dev = -1;
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
   if (dev != set_dev) {
     err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
     if (err != cudaSuccess) return err;
-    err = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    if (err != cudaSuccess) return err;
     set_dev = dev;
   }
   int per_sm = 0;
-  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, WARPS * 32, smem);
   if (err != cudaSuccess) return err;
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)nsm);
-  cfg.blockDim = dim3(kThreads);
+  cfg.gridDim = dim3((unsigned)sm_count());
+  cfg.blockDim = dim3(WARPS * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -905,6 +938,15 @@ cudaError_t launch_t(const DecodeArgs& a, size_t smem, cudaStream_t st) {
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
+template <int WARPS>
+cudaError_t launch_w(const DecodeArgs& a, size_t smem, cudaStream_t st) {
+  // the router's token loop is specialised for 1, 2, 4 or 8 tokens
+  if (a.T <= 1) return launch_t<1, WARPS>(a, smem, st);
+  if (a.T <= 2) return launch_t<2, WARPS>(a, smem, st);
+  if (a.T <= 4) return launch_t<4, WARPS>(a, smem, st);
+  return launch_t<8, WARPS>(a, smem, st);
+}
+
 }  // namespace
 
 size_t decode_smem_bytes(int T, int k, int E, int H, int I, int Is) {
@@ -912,20 +954,13 @@ size_t decode_smem_bytes(int T, int k, int E, int H, int I, int Is) {
   if (T < 1 || T > kDecodeMaxT || P > kDecodeMaxP || E < 1 || E > 512) return 0;
   // groups of 64 in pairs (the scale copies move 2 or 4 groups), whole 16-row tiles
   if (H % 128 || I % 128 || Is % 128 || H % 16) return 0;
-  const DSmem m = dsmem(T, P, E, H, I, Is);
-  if (tk_bytes(T, P, E) > m.end2 - m.tk) return 0;
-  const size_t need = m.end2 > m.end3 ? m.end2 : m.end3;
-  return need <= kMaxSmem ? need : 0;
+  return smem_for(T, k, E, H, I, Is, decode_warps(T, k, E, I, Is));
 }
 
 cudaError_t launch_decode_block(const DecodeArgs& a, cudaStream_t st) {
   const size_t smem = decode_smem_bytes(a.T, a.k, a.ta.E, a.H, a.I, a.Is);
   if (!smem) return cudaErrorInvalidValue;
-  // the router's token loop is specialised for 1, 2, 4 or 8 tokens
-  if (a.T <= 1) return launch_t<1>(a, smem, st);
-  if (a.T <= 2) return launch_t<2>(a, smem, st);
-  if (a.T <= 4) return launch_t<4>(a, smem, st);
-  return launch_t<8>(a, smem, st);
+  return decode_warps(a.T, a.k, a.ta.E, a.I, a.Is) == 16 ? launch_w<16>(a, smem, st) : launch_w<8>(a, smem, st);
 }
 
 }  // namespace moe

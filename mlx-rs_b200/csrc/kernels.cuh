@@ -182,7 +182,7 @@ cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st);
 // hidden rows.
 constexpr int kDecodeMaxT = 8;
 constexpr int kDecodeMaxP = 64;
-constexpr int kDecodeWarps = 8;
+constexpr int kDecodeWarps = 16;  // at most (8 or 16 by the number of units)
 constexpr int kDecodeLogitReplicas = 16;
 struct DecodeArgs {
   RouterArgs ra;             // logits into scratch [T, n_rows]
