@@ -193,13 +193,13 @@ MOE_DEV bool grid_barrier(uint32_t* bar, int32_t* status, int* ok_s) {
 // read through L2: other CTAs of this grid may have written them) or, with FROM_XR, from
 // the swizzled raw copy at byte offset xr of the shared array (rows of 2K bytes). Every
 // thread calls it.
-template <bool FROM_XR>
+template <bool FROM_XR, int THREADS>
 MOE_DEV void stage_rows(unsigned char* smem, uint32_t dst, float* sums, int sstride, const uint16_t* src,
                         uint32_t xr, int nrows, int K) {
   const int G = K >> 6;
   const int units = nrows * G * 4;
   const int rb = 2 * K + 16;
-  for (int u0 = 0; u0 < units; u0 += (int)blockDim.x) {  // uniform trip count (shuffles below)
+  for (int u0 = 0; u0 < units; u0 += THREADS) {  // uniform trip count (shuffles below)
     const int u = u0 + (int)threadIdx.x;
     const bool v = u < units;
     const int c = u & 3, g = (u >> 2) % G, t = (u >> 2) / G;
@@ -321,11 +321,12 @@ MOE_DEV void router_row(const RouterArgs& a, int row, const unsigned char* xr, i
 // sums experts l, l+32, ... in order, then the xor butterfly), IEEE divides and
 // roundings; the expert of rank j (the number of experts ranking before it) is the j-th
 // arg-max round's winner. sel/selw: [T*k] scratch; red: [16] floats.
+template <int THREADS>
 MOE_DEV void topk_cta(const TopkArgs& a, int T, float* vals, float* keys, float* red, int* sel, float* selw,
                       uint32_t* s_idx, uint16_t* s_w, uint16_t* s_gate, bool has_gate) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int E = a.E, n = T * E, k = a.k;
-  for (int i = tid; i < n; i += (int)blockDim.x) {
+  for (int i = tid; i < n; i += THREADS) {
     const int t = i / E, e = i - t * E;
     float v = bf2f(__ldcg(a.logits + (size_t)t * a.n_rows + e));
     if (a.scoring == 1) v = rbf(__fadd_rn(v, bf2f(a.expert_bias[e])));
@@ -348,7 +349,7 @@ MOE_DEV void topk_cta(const TopkArgs& a, int T, float* vals, float* keys, float*
       if (lane == 0) red[warp] = m;
     }
     __syncthreads();
-    for (int i = tid; i < n; i += (int)blockDim.x) vals[i] = exp_canon(__fsub_rn(vals[i], red[i / E]));
+    for (int i = tid; i < n; i += THREADS) vals[i] = exp_canon(__fsub_rn(vals[i], red[i / E]));
     __syncthreads();
     if (warp < T) {
       float sm = 0.0f;
@@ -358,7 +359,7 @@ MOE_DEV void topk_cta(const TopkArgs& a, int T, float* vals, float* keys, float*
       if (lane == 0) red[8 + warp] = sm;
     }
     __syncthreads();
-    for (int i = tid; i < n; i += (int)blockDim.x) {
+    for (int i = tid; i < n; i += THREADS) {
       const float v = rbf(__fdiv_rn(vals[i], red[8 + i / E]));
       vals[i] = v;
       keys[i] = v;
@@ -371,7 +372,7 @@ MOE_DEV void topk_cta(const TopkArgs& a, int T, float* vals, float* keys, float*
   // (index ascending among equal keys). The expert of rank r (the number of larger words
   // in its token's row) is the r-th winner of topk_token's arg-max rounds.
   uint32_t* ord = reinterpret_cast<uint32_t*>(keys);  // in place: [T][E]
-  for (int i = tid; i < n; i += (int)blockDim.x) {
+  for (int i = tid; i < n; i += THREADS) {
     const int e = i - (i / E) * E;
     const float kf = keys[i];
     uint32_t b = __float_as_uint(kf) >> 16;  // exact: keys are bf16 values
@@ -380,7 +381,7 @@ MOE_DEV void topk_cta(const TopkArgs& a, int T, float* vals, float* keys, float*
     ord[i] = (code << 16) | (0xffffu - (uint32_t)e);
   }
   __syncthreads();
-  for (int i = tid; i < n; i += (int)blockDim.x) {
+  for (int i = tid; i < n; i += THREADS) {
     const int t = i / E;
     const uint32_t* orow = ord + t * E;
     const uint32_t me = ord[i];
@@ -608,7 +609,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) decode_block_kernel(DecodeArgs 
     float* selw = reinterpret_cast<float*>(sel + P);
     TopkArgs ta = a.ta;
     ta.logits = a.logits_rep + (size_t)(blockIdx.x % kDecodeLogitReplicas) * T * ta.n_rows;
-    topk_cta(ta, T, vals, keys, red, sel, selw, s_idx, s_w, s_gate, a.has_gate != 0);
+    topk_cta<kThreads>(ta, T, vals, keys, red, sel, selw, s_idx, s_w, s_gate, a.has_gate != 0);
   }
   if (warp == 0) {
     // position of pair p in (expert, p) order
@@ -655,7 +656,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) decode_block_kernel(DecodeArgs 
   const int U = s_U;
 
   // ---- phase 2: gate/up + SwiGLU of the selected experts and the shared expert
-  stage_rows<true>(smem, L.x, reinterpret_cast<float*>(smem + L.xsum), 8, nullptr, L.xr, T, H);
+  stage_rows<true, kThreads>(smem, L.x, reinterpret_cast<float*>(smem + L.xsum), 8, nullptr, L.xr, T, H);
   {
     // this CTA's slice of every selected expert's down weights (and of the shared down)
     // into L2: the down projection after the next barrier reads L2, not HBM. One thread
@@ -757,8 +758,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) decode_block_kernel(DecodeArgs 
 
   // ---- phase 3: down projection + combine, CTA = tiles of 16 hidden rows
   if (blockIdx.x * 16 >= H) return;
-  stage_rows<false>(smem, L.h, reinterpret_cast<float*>(smem + L.hsum), P, a.hbuf, 0, P, I);
-  if (Is) stage_rows<false>(smem, L.hs, reinterpret_cast<float*>(smem + L.hssum), 8, a.hsbuf, 0, T, Is);
+  stage_rows<false, kThreads>(smem, L.h, reinterpret_cast<float*>(smem + L.hsum), P, a.hbuf, 0, P, I);
+  if (Is) stage_rows<false, kThreads>(smem, L.hs, reinterpret_cast<float*>(smem + L.hssum), 8, a.hsbuf, 0, T, Is);
   __syncthreads();
   float* prod = reinterpret_cast<float*>(smem + L.prod);
   float* spart = reinterpret_cast<float*>(smem + L.spart);
